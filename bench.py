@@ -1,0 +1,379 @@
+#!/usr/bin/env python
+"""Decode benchmark of the B200 Q4_K decoder path.
+
+Workload (default): Llama-2-7B-shape decoder (32 layers, d 4096, 32 heads x
+128, SwiGLU 11008, vocab 32000, RMSNorm eps 1e-5, RoPE theta 1e4), every
+linear Q4_K with seeded random fields, f32 N(0, 0.02) token embedding and
+output norm, batch 1. The KV cache is filled by decoding 2048 random token
+ids, then W warm-up and K timed greedy tokens run as CUDA-graph replays.
+
+value      tokens/s over the K timed tokens (CUDA events on the decode
+           stream, max over ranks), weights and KV resident in HBM
+           (3.7 GB of weights per token: far larger than L2).
+e2e        tokens/s through the public API with host buffers: per token
+           position_logits (device->host copy of the logits), host argmax
+           over non-EOG ids, push_token (host->device copy of the id).
+roofline   the Q4_K dequant-GEMV (the dominant kernel) over this rank's
+           7B layer shapes + head, replayed in a CUDA graph over three
+           weight copies per shape (411 MB > L2), CUDA events.
+cpu_baseline  the C++ oracle restatement of the reference's CPU path on
+           this host's cores: a 2-layer sample of the same model at
+           context 2048, extrapolated to 32 layers.
+
+--impl reference times that CPU path as its own line (the reference is
+Rust with no toolchain here; its restatement is the oracle port).
+Multi-GPU (torchrun): tensor parallel over N ranks with NCCL all-reduce
+after the O and down projections; same tokens on every rank.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode tok/s (7B-shape Q4_K, bs1) and Q4_K GEMV HBM GB/s vs peak"
+SEED = 20261201
+PREFILL = 2048
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for k, nm in enumerate(names):
+                if len(r) > 5 + k and r[5 + k].strip() == "Active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def build_model(cfg, device, tp, rank, uid):
+    from faber_runtime_b200 import DeviceModel, synth
+    return DeviceModel(cfg, synth.model_tensors(cfg, SEED), device=device, tp_size=tp,
+                       tp_rank=rank, nccl_uid=uid)
+
+
+def gemv_roofline(cfg, tp, stream_ptr, reps=6):
+    """Dominant kernel: the tiled Q4_K GEMV over this rank's decode shapes."""
+    import torch
+    from faber_runtime_b200 import dequant, synth
+    d, hd, F = cfg.d_model, cfg.head_dim, cfg.ffn
+    Fl = (F // 256) // tp * 256 if tp > 1 else F
+    shapes = [("qkv", (cfg.n_heads + 2 * cfg.n_kv_heads) * hd // tp, d), ("o", d, cfg.n_heads * hd // tp),
+              ("gateup", 2 * Fl, d), ("down", d, Fl), ("head", cfg.vocab // tp, d)]
+    copies = 3
+    tens, bytes_per_round = [], 0
+    for name, r, c in shapes:
+        for k in range(copies):
+            blocks = synth.q4k_blocks(SEED + k, synth.stream_id(name) + k, r * c // 256)
+            tens.append((dequant.Q4kTensor(blocks, r, c), r, c))
+            bytes_per_round += r * c * 144 // 256 + 4 * c + 4 * r
+    xmax = max(c for _, _, c in tens)
+    x = torch.randn(xmax, device="cuda")
+    y = torch.empty(max(r for _, r, _ in tens), device="cuda")
+    s = torch.cuda.current_stream()
+    for t, r, c in tens:  # warm (and set kernel attributes) outside capture
+        t.gemv(x.data_ptr(), y.data_ptr(), s.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cs = torch.cuda.current_stream().cuda_stream
+        for _ in range(reps):
+            for t, r, c in tens:
+                t.gemv(x.data_ptr(), y.data_ptr(), cs)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = 3 * reps * len(tens)
+    total_bytes = 3 * reps * bytes_per_round
+    # C0 shape alone (4096 x 4096, 9 469 952 B per matvec), 16 copies (151 MB)
+    c0 = [dequant.Q4kTensor(synth.q4k_blocks(SEED, 900 + k, 65536), 4096, 4096) for k in range(16)]
+    for t in c0:
+        t.gemv(x.data_ptr(), y.data_ptr(), s.cuda_stream)
+    torch.cuda.synchronize()
+    g0 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g0):
+        cs = torch.cuda.current_stream().cuda_stream
+        for _ in range(8):
+            for t in c0:
+                t.gemv(x.data_ptr(), y.data_ptr(), cs)
+    g0.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(3):
+        g0.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms0 = e0.elapsed_time(e1)
+    n0 = 3 * 8 * 16
+    return {"launches": launches, "avg_us": ms * 1e3 / launches, "bytes_per_launch": total_bytes / launches,
+            "achieved_gbs": total_bytes / (ms * 1e-3) / 1e9,
+            "c0_us": ms0 * 1e3 / n0, "c0_gbs": 9469952 * n0 / (ms0 * 1e-3) / 1e9}
+
+
+def cpu_sample(cfg, threads=None):
+    """The oracle on this host's cores: 2 layers of cfg at context 2048,
+    one token (push + logits), extrapolated to cfg.n_layers."""
+    import oracle
+    from faber_runtime_b200 import synth
+    threads = threads or os.cpu_count() or 1
+    oracle.set_threads(threads)
+    sub = cfg.with_layers(2)
+    tensors = {n: (t, a, r, c) for n, t, a, r, c in synth.model_tensors(sub, SEED)}
+    om = oracle.OracleModel(sub, tensors)
+    span = cfg.n_kv_heads * cfg.head_dim
+    run = oracle.OracleRun(om, PREFILL + 64)
+    for layer in range(2):
+        k = synth.normal(SEED, 5000 + layer, PREFILL * span, 0.0, 50.0)
+        v = synth.normal(SEED, 6000 + layer, PREFILL * span, 0.0, 50.0)
+        run.set_prefix(layer, k, v, PREFILL)
+    tok = 1
+    times = []
+    t_end = time.perf_counter() + 20.0
+    while True:
+        t0 = time.perf_counter()
+        run.push_token(tok)
+        t1 = time.perf_counter()
+        logits = run.position_logits()
+        t2 = time.perf_counter()
+        tok = oracle.top1_non_eog(logits)
+        times.append((t1 - t0, t2 - t1))
+        if len(times) >= 2 and time.perf_counter() > t_end or len(times) >= 8:
+            break
+    push = float(np.median([a for a, _ in times]))
+    head = float(np.median([b for _, b in times]))
+    per_token = push * cfg.n_layers / 2 + head
+    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"C++ oracle, {cfg.name} cut to 2 of {cfg.n_layers} layers at context {PREFILL}, "
+                      f"{len(times)} tokens (push {push:.3f} s + logits {head:.3f} s), per-token time "
+                      f"extrapolated as push*{cfg.n_layers // 2} + logits",
+            "per_token_s": per_token}
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    from faber_runtime_b200 import LLAMA2_7B
+    cfg = LLAMA2_7B
+    if rank != 0:
+        return
+    # each step: one oracle decode token through a 2-layer sample, scaled
+    import oracle
+    from faber_runtime_b200 import synth
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    sub = cfg.with_layers(2)
+    om = oracle.OracleModel(sub, {n: (t, a, r, c) for n, t, a, r, c in synth.model_tensors(sub, SEED)})
+    span = cfg.n_kv_heads * cfg.head_dim
+    total = PREFILL + args.warmup + args.steps + 8
+    run = oracle.OracleRun(om, total)
+    for layer in range(2):
+        run.set_prefix(layer, synth.normal(SEED, 5000 + layer, PREFILL * span, 0.0, 50.0),
+                       synth.normal(SEED, 6000 + layer, PREFILL * span, 0.0, 50.0), PREFILL)
+    tok = 1
+
+    def step():
+        nonlocal tok
+        t0 = time.perf_counter()
+        run.push_token(tok)
+        t1 = time.perf_counter()
+        lg = run.position_logits()
+        t2 = time.perf_counter()
+        tok = oracle.top1_non_eog(lg)
+        return (t1 - t0) * cfg.n_layers / 2 + (t2 - t1)
+
+    for _ in range(args.warmup):
+        step()
+    per = [step() for _ in range(args.steps)]
+    per_token = float(np.sum(per))
+    value = args.steps / per_token
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_token / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Q4_K fields, random token ids)",
+            "config": {"workload": f"{cfg.name} greedy decode, batch 1, context {PREFILL}",
+                       "global_batch": 1, "seq_len": PREFILL, "parallelism": "cpu",
+                       "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"C++ oracle restatement (the Rust reference has no toolchain here), "
+                                       f"2 of {cfg.n_layers} layers at context {PREFILL} per step, "
+                                       f"time scaled x{cfg.n_layers // 2} plus the head"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_faber(args):
+    import torch
+    ws, rank, local = dist_env()
+    n = args.gpus
+    torch.cuda.set_device(local)
+    from faber_runtime_b200 import LLAMA2_7B, ForwardRun, _lib, synth, top1_non_eog
+    cfg = LLAMA2_7B
+    uid = b""
+    pg = None
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+        pg = dist
+        buf = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            u = (ctypes_uid())
+            buf = torch.frombuffer(bytearray(u), dtype=torch.uint8)
+        dist.broadcast(buf, 0)
+        uid = bytes(buf.tolist())
+    model = build_model(cfg, local, ws, rank, uid)
+    ctx = PREFILL + args.warmup + args.steps + args.e2e_steps + 16
+    run = ForwardRun(model, context_length=ctx)
+    prompt = synth.tokens(SEED, 1, PREFILL, cfg.vocab)
+    run.push_tokens(prompt)
+    run.greedy(args.warmup)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    with Clocks(local) as clk:
+        toks, finite = run.greedy(args.steps)
+        torch.cuda.synchronize()
+    ms = run.last_greedy_ms()
+    if pg:
+        t = torch.tensor([ms], dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    value = args.steps / (ms * 1e-3)
+    # end to end through the public API with host buffers
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        lg = run.position_logits()
+        run.push_token(top1_non_eog(lg))
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if pg:
+        t = torch.tensor([wall], dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        wall = float(t.item())
+    e2e = args.e2e_steps / wall
+    roof = gemv_roofline(cfg, ws, torch.cuda.current_stream().cuda_stream)
+    peak, peak_kind = peaks()
+    step_bytes = (cfg.linear_bytes() + cfg.head_bytes()) / ws + \
+        cfg.kv_bytes_per_position() * (PREFILL + args.warmup + args.steps / 2) / ws
+    launches_per_token = (5 * cfg.n_layers + 3) if ws == 1 else (5 * cfg.n_layers + 3)
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Q4_K fields, random token ids)",
+            "config": {"workload": f"{cfg.name} greedy decode, batch 1, KV prefilled to {PREFILL} by decoding "
+                                   f"random ids, {args.steps} timed tokens",
+                       "global_batch": 1, "seq_len": PREFILL, "parallelism": f"tp{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (3.7 GB weights per token)", "kv_dtype": "f16 (value-identical)"},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * cfg.vocab},
+            "gpu_launches": launches_per_token * args.steps,
+            "roofline": {"bound": "hbm", "achieved": roof["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": roof["achieved_gbs"] / peak, "peak_kind": peak_kind,
+                         "traffic": None, "kernel": "gemv_kernel<tiled,plain,store> over 7B decode shapes",
+                         "avg_launch_us": roof["avg_us"], "bytes_per_launch": roof["bytes_per_launch"]},
+            "gemv_4096x4096": {"us": roof["c0_us"], "gbs": roof["c0_gbs"], "frac": roof["c0_gbs"] / peak},
+            "decode_step_gbs": step_bytes / (ms / args.steps * 1e-3) / 1e9,
+            "greedy_all_finite": bool(finite),
+            "clocks": clk.summary()}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(cfg)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    run.close()
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def ctypes_uid() -> bytes:
+    import ctypes
+    from faber_runtime_b200 import _lib
+    b = (ctypes.c_uint8 * 128)()
+    _lib.call("faber_gpu_v2_nccl_unique_id", ctypes.addressof(b))
+    return bytes(b)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--impl", default="faber", choices=["faber", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_faber(args)
+
+
+if __name__ == "__main__":
+    main()

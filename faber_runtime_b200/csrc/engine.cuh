@@ -1,0 +1,1046 @@
+// engine.cuh — model + session: the device analogue of CpuOracle / ForwardRun
+// / run_greedy (src/cpu_oracle.rs:409-445, 808-926; src/greedy_run.rs:186-248)
+// under the session contract of src/session.rs.
+//
+// One decode step ("push") is, per layer:
+//   QKV GEMV  [rms_norm(attn_norm) prologue | RoPE + f16 KV append epilogue]
+//   attention [split-K over positions, last CTA merges]
+//   O GEMV    [residual epilogue]            (TP: store + NCCL all-reduce)
+//   GATEUP    [rms_norm(ffn_norm) prologue | SwiGLU epilogue]
+//   DOWN GEMV [residual epilogue]            (TP: store + NCCL all-reduce)
+// and "logits" is the head GEMV [rms_norm(output_norm) | logits + argmax]
+// plus a one-thread finalize. Both are captured once per session as CUDA
+// graphs (positions and tokens live in device memory), with programmatic
+// dependent launch so each kernel's weight loads overlap its predecessor.
+#pragma once
+
+#include <nccl.h>
+
+#include <cmath>
+#include <map>
+#include <string>
+#include <vector>
+
+namespace faber {
+
+// f32 -> f16 (RN-even) on the host; finite inputs and overflow to inf.
+inline uint16_t host_f32_to_f16(float x) {
+  uint32_t b;
+  std::memcpy(&b, &x, 4);
+  const uint32_t sign = (b >> 16) & 0x8000u;
+  const uint32_t a = b & 0x7fffffffu;
+  if (a > 0x7f800000u) return (uint16_t)(sign | 0x7e00u);  // NaN
+  if (a >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u);
+  if (a >= 0x38800000u) {
+    const uint32_t e = (a >> 23) - 112u;
+    const uint32_t mant = a & 0x7fffffu;
+    uint32_t h = (e << 10) | (mant >> 13);
+    const uint32_t rest = mant & 0x1fffu;
+    if (rest > 0x1000u || (rest == 0x1000u && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+  }
+  float f;
+  std::memcpy(&f, &a, 4);
+  const double scaled = (double)f * 16777216.0;
+  double fl = std::floor(scaled);
+  const double fr = scaled - fl;
+  if (fr > 0.5 || (fr == 0.5 && std::fmod(fl, 2.0) != 0.0)) fl += 1.0;
+  return (uint16_t)(sign | (uint32_t)fl);
+}
+
+inline float host_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+  uint32_t b;
+  if (e == 0) {
+    if (m == 0) {
+      b = sign;
+    } else {
+      int p = 31 - __builtin_clz(m);  // leading bit position
+      b = sign | ((uint32_t)(p + 103) << 23) | ((m << (23 - p)) & 0x7fffffu);
+    }
+  } else if (e == 31) {
+    b = sign | 0x7f800000u | (m << 13);
+  } else {
+    b = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+inline float host_f16_round(float x) { return host_f16_to_f32(host_f32_to_f16(x)); }
+
+#define FABER_NCCL(expr)                                                                   \
+  do {                                                                                     \
+    ncclResult_t r_ = (expr);                                                              \
+    if (r_ != ncclSuccess)                                                                 \
+      throw ::faber::Error(FABER_STATUS_IO_ERROR,                                          \
+                           std::string(#expr) + " failed: " + ncclGetErrorString(r_));     \
+  } while (0)
+
+struct HostTensor {
+  uint32_t type = 0;
+  std::vector<uint8_t> bytes;  // this rank's shard, native layout
+  uint64_t rows = 0, cols = 0; // shard shape
+  bool set = false;
+};
+
+enum LayerSlot { LS_ATTN_NORM, LS_Q, LS_K, LS_V, LS_O, LS_FFN_NORM, LS_GATE, LS_UP, LS_DOWN, LS_N };
+static const char* kLayerSlotNames[LS_N] = {"attn_norm", "attn_q", "attn_k", "attn_v",
+                                            "attn_output", "ffn_norm", "ffn_gate", "ffn_up",
+                                            "ffn_down"};
+
+struct LayerDev {
+  DeviceTiled qkv, o, gateup, down;
+  DevBuf attn_norm, ffn_norm;
+};
+
+struct ModelState {
+  FaberModelConfigV1 cfg{};
+  int tp = 1, rank = 0;
+  // local (per-rank) sizes
+  int Hl = 0, Hkvl = 0, Fl = 0, Vl = 0, v0 = 0;
+  int f_blk0 = 0, f_blk1 = 0;  // this rank's FFN super-block range
+  std::vector<std::array<HostTensor, LS_N>> staged;
+  HostTensor st_embd, st_out_norm, st_output;
+  bool finalized = false;
+  std::vector<LayerDev> layers;
+  DevBuf embd_f16;   // [V][d] f16 (f16-rounded token_embd)
+  DevBuf out_norm;   // [d] f32, not rounded
+  DeviceTiled head;  // untied Q4_K head, local vocab rows
+  ncclComm_t comm = nullptr;
+  int device = 0;
+  uint64_t device_bytes = 0;
+  ~ModelState() {
+    if (comm) ncclCommDestroy(comm);
+  }
+};
+
+}  // namespace faber
+
+struct FaberGpuModel {
+  faber::ModelState s;
+};
+
+namespace faber {
+
+struct SessionState {
+  FaberGpuModel* m = nullptr;
+  FaberKvLayoutV1 kv{};
+  int max_ctx = 0;
+  int max_splits = 0;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  DevBuf kcache, vcache;  // [L][ctx][Hkvl*hd] f16
+  DevBuf rope;            // [ctx][hd/2] float2
+  DevBuf h, h2, q, ctx, hh, logits, logits_full, opart, dpart;
+  DevBuf attn_part, attn_counters;
+  DevBuf state;           // StepState
+  DevBuf gen;             // int64 [max_ctx]
+  DevBuf prompt;          // int64 staging for pushes
+  int64_t* pinned = nullptr;  // pinned host staging
+  size_t pinned_n = 0;
+  uint64_t n = 0;         // host mirror of the sequence length
+  bool prefix_pending = false;
+  uint64_t prefix_n = 0;
+  std::vector<uint8_t> prefix_layers;
+  // graphs
+  cudaGraphExec_t g_push = nullptr, g_logits = nullptr, g_step = nullptr;
+  std::vector<int64_t> graph_eog;
+  bool graphs_valid = false;
+  // tracing (eager path)
+  bool trace = false;
+  DevBuf tr;  // [L][8][maxw] f32
+  int tr_w = 0;
+  // timing
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_greedy_ms = 0.f;
+  // commit contract (src/session.rs:422-456)
+  uint32_t c_position = 0;
+  uint64_t c_kv_generations = 0;
+  std::vector<int64_t> c_history;
+
+  ~SessionState() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    destroy_graphs();
+    if (pinned) cudaFreeHost(pinned);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    if (cur >= 0) cudaSetDevice(cur);
+  }
+  void destroy_graphs() {
+    if (g_push) cudaGraphExecDestroy(g_push);
+    if (g_logits) cudaGraphExecDestroy(g_logits);
+    if (g_step) cudaGraphExecDestroy(g_step);
+    g_push = g_logits = g_step = nullptr;
+    graphs_valid = false;
+  }
+};
+
+}  // namespace faber
+
+struct FaberGpuSession {
+  faber::SessionState s;
+};
+
+namespace faber {
+
+// ---------------------------------------------------------------------------
+// Model construction
+// ---------------------------------------------------------------------------
+inline void validate_config(const FaberModelConfigV1& c) {
+  FABER_ARG(c.n_layers > 0 && c.d_model > 0 && c.n_heads > 0 && c.n_kv_heads > 0 &&
+                c.head_dim > 0 && c.ffn > 0 && c.vocab > 0,
+            "zero-sized model dimension");
+  FABER_ARG(c.n_heads % c.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads");
+  require(c.head_dim == 64 || c.head_dim == 128, FABER_STATUS_UNSUPPORTED, "head_dim must be 64 or 128");
+  require(c.n_heads / c.n_kv_heads <= (uint32_t)kAttnMaxRatio, FABER_STATUS_UNSUPPORTED,
+          "GQA ratio above 8");
+  require(c.d_model % 256 == 0, FABER_STATUS_UNSUPPORTED, "d_model must be a multiple of 256");
+  require(c.ffn % 32 == 0, FABER_STATUS_UNSUPPORTED, "ffn must be a multiple of 32");
+  FABER_ARG(c.tp_size >= 1 && c.tp_rank < c.tp_size, "bad tensor-parallel rank");
+  if (c.tp_size > 1) {
+    require(c.n_heads % c.tp_size == 0 && c.n_kv_heads % c.tp_size == 0, FABER_STATUS_UNSUPPORTED,
+            "heads must divide evenly across tensor-parallel ranks");
+    require(c.ffn % 256 == 0 && c.ffn / 256 >= c.tp_size, FABER_STATUS_UNSUPPORTED,
+            "ffn must be whole super-blocks, at least one per rank");
+  }
+}
+
+// Native block sub-tensor [r0, r0+nr) x [c0, c0+nc) of a [rows][cols] Q4_K
+// tensor (c0, nc multiples of 256, cols % 256 == 0).
+inline std::vector<uint8_t> q4k_shard(const uint8_t* src, uint64_t cols, uint64_t r0, uint64_t nr,
+                                      uint64_t c0, uint64_t nc) {
+  const uint64_t nbr = cols / 256, b0 = c0 / 256, nbl = nc / 256;
+  std::vector<uint8_t> out(nr * nbl * kQ4kBlockBytes);
+  for (uint64_t r = 0; r < nr; ++r)
+    std::memcpy(out.data() + r * nbl * kQ4kBlockBytes,
+                src + ((r0 + r) * nbr + b0) * kQ4kBlockBytes, nbl * kQ4kBlockBytes);
+  return out;
+}
+
+inline void model_set_tensor(ModelState& M, const std::string& name, uint32_t type,
+                             const void* data, uint64_t nbytes, uint64_t rows, uint64_t cols) {
+  const FaberModelConfigV1& c = M.cfg;
+  FABER_ARG(!M.finalized, "model already finalized");
+  FABER_ARG(data != nullptr || nbytes == 0, "null tensor data");
+  const uint64_t d = c.d_model, hd = c.head_dim;
+  auto expect_shape = [&](uint64_t er, uint64_t ec) {
+    FABER_ARG(rows == er && cols == ec, name + ": shape [" + std::to_string(rows) + "x" +
+                                            std::to_string(cols) + "], expected [" +
+                                            std::to_string(er) + "x" + std::to_string(ec) + "]");
+  };
+  auto expect_bytes = [&](uint64_t want) {
+    FABER_ARG(nbytes == want, name + ": packed tensor is " + std::to_string(nbytes) +
+                                  " bytes, expected exactly " + std::to_string(want));
+  };
+  auto f32_vec = [&](HostTensor& h, uint64_t n) {
+    require(type == FABER_GGML_F32, FABER_STATUS_UNSUPPORTED, name + ": expected F32");
+    expect_shape(n, 1);
+    expect_bytes(n * 4);
+    h.type = type;
+    h.rows = n;
+    h.cols = 1;
+    h.bytes.assign(static_cast<const uint8_t*>(data), static_cast<const uint8_t*>(data) + nbytes);
+    h.set = true;
+  };
+  const uint8_t* src = static_cast<const uint8_t*>(data);
+  // Q4_K linear; shard rows [r0, r0+nr) and cols [c0, c0+nc) for this rank.
+  auto q4k = [&](HostTensor& h, uint64_t er, uint64_t ec, uint64_t r0, uint64_t nr, uint64_t c0,
+                 uint64_t nc) {
+    require(type == FABER_GGML_Q4_K, FABER_STATUS_UNSUPPORTED,
+            name + ": only Q4_K linears are supported on this path");
+    expect_shape(er, ec);
+    FABER_ARG((er * ec) % 256 == 0, name + ": element count not a multiple of 256");
+    expect_bytes(er * ec / 256 * kQ4kBlockBytes);
+    h.type = type;
+    if (M.tp == 1) {
+      h.bytes.assign(src, src + nbytes);
+      h.rows = er;
+      h.cols = ec;
+    } else {
+      h.bytes = q4k_shard(src, ec, r0, nr, c0, nc);
+      h.rows = nr;
+      h.cols = nc;
+    }
+    h.set = true;
+  };
+  if (name == "token_embd.weight") {
+    require(type == FABER_GGML_F32, FABER_STATUS_UNSUPPORTED, name + ": expected F32");
+    expect_shape(c.vocab, d);
+    expect_bytes((uint64_t)c.vocab * d * 4);
+    M.st_embd.type = type;
+    M.st_embd.rows = c.vocab;
+    M.st_embd.cols = d;
+    M.st_embd.bytes.assign(src, src + nbytes);
+    M.st_embd.set = true;
+    return;
+  }
+  if (name == "output_norm.weight") return f32_vec(M.st_out_norm, d);
+  if (name == "output.weight") {
+    FABER_ARG(!c.tied_head, "output.weight given for a tied-head model");
+    return q4k(M.st_output, c.vocab, d, M.v0, M.Vl, 0, d);
+  }
+  // blk.N.slot.weight
+  unsigned layer = 0;
+  char slot[64] = {0};
+  FABER_ARG(std::sscanf(name.c_str(), "blk.%u.%63[a-z_].weight", &layer, slot) == 2 &&
+                layer < c.n_layers,
+            "unknown tensor name " + name);
+  int ls = -1;
+  for (int k = 0; k < LS_N; ++k)
+    if (std::string(slot) == kLayerSlotNames[k]) ls = k;
+  FABER_ARG(ls >= 0, "unknown tensor name " + name);
+  HostTensor& h = M.staged[layer][(size_t)ls];
+  const uint64_t H = c.n_heads, Hkv = c.n_kv_heads, F = c.ffn;
+  const uint64_t fr0 = (uint64_t)M.f_blk0 * 256, fnr = (uint64_t)(M.f_blk1 - M.f_blk0) * 256;
+  switch (ls) {
+    case LS_ATTN_NORM:
+    case LS_FFN_NORM: return f32_vec(h, d);
+    case LS_Q: return q4k(h, H * hd, d, M.rank * M.Hl * hd, M.Hl * hd, 0, d);
+    case LS_K:
+    case LS_V: return q4k(h, Hkv * hd, d, M.rank * M.Hkvl * hd, M.Hkvl * hd, 0, d);
+    case LS_O: return q4k(h, d, H * hd, 0, d, M.rank * M.Hl * hd, M.Hl * hd);
+    case LS_GATE:
+    case LS_UP: return q4k(h, F, d, fr0, fnr, 0, d);
+    case LS_DOWN: return q4k(h, d, F, 0, d, fr0, fnr);
+  }
+}
+
+inline uint64_t nblk(const HostTensor& h) { return h.rows * h.cols / 256; }
+
+inline void model_finalize(ModelState& M) {
+  const FaberModelConfigV1& c = M.cfg;
+  FABER_ARG(!M.finalized, "model already finalized");
+  // coverage: every tensor present (src/cpu_oracle.rs:409-445)
+  FABER_ARG(M.st_embd.set, "missing tensor token_embd.weight");
+  FABER_ARG(M.st_out_norm.set, "missing tensor output_norm.weight");
+  FABER_ARG(c.tied_head || M.st_output.set, "missing tensor output.weight");
+  for (uint32_t l = 0; l < c.n_layers; ++l)
+    for (int k = 0; k < LS_N; ++k)
+      FABER_ARG(M.staged[l][(size_t)k].set,
+                "missing tensor blk." + std::to_string(l) + "." + kLayerSlotNames[k] + ".weight");
+  FABER_CUDA(cudaSetDevice(M.device));
+  const uint64_t d = c.d_model, hd = c.head_dim;
+  M.layers.resize(c.n_layers);
+  uint64_t bytes = 0;
+  for (uint32_t l = 0; l < c.n_layers; ++l) {
+    auto& S = M.staged[l];
+    LayerDev& L = M.layers[l];
+    const uint64_t nq = (uint64_t)M.Hl * hd, nk = (uint64_t)M.Hkvl * hd;
+    // fused QKV: rows [q | k | v]
+    L.qkv.from(repack_q4k((int)(nq + 2 * nk), (int)d, [&](int j) {
+      const HostTensor& t = (uint64_t)j < nq ? S[LS_Q] : ((uint64_t)j < nq + nk ? S[LS_K] : S[LS_V]);
+      const uint64_t r = (uint64_t)j < nq ? j : ((uint64_t)j < nq + nk ? j - nq : j - nq - nk);
+      return RowSeg{t.bytes.data(), nblk(t), r * d};
+    }));
+    L.o.from(repack_q4k((int)d, (int)S[LS_O].cols, [&](int j) {
+      return RowSeg{S[LS_O].bytes.data(), nblk(S[LS_O]), (uint64_t)j * S[LS_O].cols};
+    }));
+    // gate/up interleaved: row 2f = gate f, 2f+1 = up f (SwiGLU epilogue pairs)
+    const uint64_t Fl = S[LS_GATE].rows;
+    L.gateup.from(repack_q4k((int)(2 * Fl), (int)d, [&](int j) {
+      const HostTensor& t = (j & 1) ? S[LS_UP] : S[LS_GATE];
+      return RowSeg{t.bytes.data(), nblk(t), (uint64_t)(j >> 1) * d};
+    }));
+    L.down.from(repack_q4k((int)d, (int)S[LS_DOWN].cols, [&](int j) {
+      return RowSeg{S[LS_DOWN].bytes.data(), nblk(S[LS_DOWN]), (uint64_t)j * S[LS_DOWN].cols};
+    }));
+    // per-layer norms are f16-rounded like every per-layer tensor
+    // (src/cpu_oracle.rs:323-331)
+    for (int k : {LS_ATTN_NORM, LS_FFN_NORM}) {
+      std::vector<float> w(d);
+      std::memcpy(w.data(), S[(size_t)k].bytes.data(), d * 4);
+      for (auto& v : w) v = host_f16_round(v);
+      upload(k == LS_ATTN_NORM ? L.attn_norm : L.ffn_norm, w.data(), d * 4);
+    }
+    bytes += L.qkv.w.n + L.o.w.n + L.gateup.w.n + L.down.w.n + 2 * d * 4;
+    for (auto& t : S) {
+      std::vector<uint8_t>().swap(t.bytes);
+    }
+  }
+  // token_embd stored as f16 (its f16 rounding, src/cpu_oracle.rs:420-421)
+  {
+    const float* e = reinterpret_cast<const float*>(M.st_embd.bytes.data());
+    const uint64_t n = (uint64_t)c.vocab * d;
+    std::vector<uint16_t> h(n);
+    for (uint64_t i = 0; i < n; ++i) h[i] = host_f32_to_f16(e[i]);
+    upload(M.embd_f16, h.data(), n * 2);
+    bytes += n * 2;
+    std::vector<uint8_t>().swap(M.st_embd.bytes);
+  }
+  upload(M.out_norm, M.st_out_norm.bytes.data(), d * 4);  // not rounded (src/cpu_oracle.rs:434)
+  if (!c.tied_head) {
+    M.head.from(repack_q4k((int)M.st_output.rows, (int)d, [&](int j) {
+      return RowSeg{M.st_output.bytes.data(), nblk(M.st_output), (uint64_t)j * d};
+    }));
+    bytes += M.head.w.n;
+    std::vector<uint8_t>().swap(M.st_output.bytes);
+  }
+  M.device_bytes = bytes;
+  M.finalized = true;
+}
+
+// ---------------------------------------------------------------------------
+// Session
+// ---------------------------------------------------------------------------
+inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV1& kv) {
+  ModelState& M = m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  FABER_ARG(M.finalized, "model not finalized");
+  FABER_ARG(kv.slots == 1, "one sequence slot per session");
+  FABER_ARG(kv.context_length > 0 && kv.layer_count == c.n_layers &&
+                kv.kv_head_count == c.n_kv_heads && kv.head_dim == c.head_dim,
+            "KV layout does not match the model");
+  require(kv.dtype == 1, FABER_STATUS_UNSUPPORTED,
+          "the device KV cache stores f16 (dtype 1); every cached K/V is an f16-rounded value");
+  S.m = m;
+  S.kv = kv;
+  S.device = M.device;
+  FABER_CUDA(cudaSetDevice(M.device));
+  S.max_ctx = (int)kv.context_length;
+  S.max_splits = (S.max_ctx + kAttnChunk - 1) / kAttnChunk;
+  const uint64_t hd = c.head_dim, d = c.d_model;
+  const uint64_t kvs = (uint64_t)M.Hkvl * hd;
+  const uint64_t cache = (uint64_t)c.n_layers * S.max_ctx * kvs * 2;
+  S.kcache.alloc(cache);
+  S.vcache.alloc(cache);
+  FABER_CUDA(cudaMemset(S.kcache.p, 0, cache));
+  FABER_CUDA(cudaMemset(S.vcache.p, 0, cache));
+  // RoPE table on the host with the same libm calls as rope_norm
+  // (src/decoder_ops.rs:178-186): theta = pos * base^(-(2k)/dim).
+  {
+    std::vector<float2> t((size_t)S.max_ctx * (hd / 2));
+    for (int p = 0; p < S.max_ctx; ++p)
+      for (uint64_t k = 0; k < hd / 2; ++k) {
+        const float theta = (float)p * powf(c.rope_theta, -(2.0f * (float)k) / (float)hd);
+        t[(size_t)p * (hd / 2) + k] = make_float2(cosf(theta), sinf(theta));
+      }
+    upload(S.rope, t.data(), t.size() * sizeof(float2));
+  }
+  const uint64_t qn = (uint64_t)M.Hl * hd;
+  S.h.alloc(d * 4);
+  S.h2.alloc(d * 4);
+  S.opart.alloc(d * 4);
+  S.dpart.alloc(d * 4);
+  S.q.alloc(qn * 4);
+  S.ctx.alloc(qn * 4);
+  S.hh.alloc((uint64_t)M.Fl * 4);
+  S.logits.alloc((uint64_t)M.Vl * 4);
+  if (M.tp > 1) S.logits_full.alloc((uint64_t)c.vocab * 4);
+  S.attn_part.alloc((uint64_t)M.Hl * S.max_splits * (hd + 2) * 4);
+  S.attn_counters.alloc((uint64_t)M.Hkvl * 4);
+  FABER_CUDA(cudaMemset(S.attn_counters.p, 0, S.attn_counters.n));
+  S.state.alloc(sizeof(StepState));
+  StepState st = {};
+  st.finite = 1;
+  FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
+  S.gen.alloc((uint64_t)S.max_ctx * 8 + 8);
+  S.prompt.alloc((uint64_t)S.max_ctx * 8);
+  FABER_CUDA(cudaStreamCreateWithFlags(&S.stream, cudaStreamNonBlocking));
+  FABER_CUDA(cudaEventCreate(&S.ev0));
+  FABER_CUDA(cudaEventCreate(&S.ev1));
+  FABER_CUDA(cudaMallocHost(&S.pinned, 4096 * sizeof(int64_t)));
+  S.pinned_n = 4096;
+  S.prefix_layers.assign(c.n_layers, 0);
+}
+
+inline StepState* st_ptr(SessionState& S) { return S.state.as<StepState>(); }
+
+// Enqueue one push step (embedding + all layers) on S.stream.
+inline void enqueue_push(SessionState& S, bool pdl) {
+  ModelState& M = S.m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  const int d = (int)c.d_model, hd = (int)c.head_dim;
+  const int nq = M.Hl * hd, nk = M.Hkvl * hd;
+  const size_t layer_cache = (size_t)S.max_ctx * nk;
+  StepState* st = st_ptr(S);
+  launch_pdl(embed_kernel, dim3(1), dim3(256), 0, S.stream, pdl, st,
+             (const __half*)M.embd_f16.as<__half>(), d, (int)c.vocab, S.h.as<float>());
+  for (uint32_t l = 0; l < c.n_layers; ++l) {
+    LayerDev& L = M.layers[l];
+    float* tr = S.trace ? S.tr.as<float>() + (size_t)l * 8 * S.tr_w : nullptr;
+    // QKV
+    {
+      GemvArgs a = L.qkv.args();
+      a.norm_w = L.attn_norm.as<float>();
+      a.eps = c.rms_eps;
+      a.q_out = S.q.as<float>();
+      a.k_cache = S.kcache.as<__half>() + l * layer_cache;
+      a.v_cache = S.vcache.as<__half>() + l * layer_cache;
+      a.rope = S.rope.as<float2>();
+      a.pos_ptr = &st->cur_pos;
+      a.nq = nq;
+      a.nk = nk;
+      a.head_dim = hd;
+      if (tr) {
+        a.x_norm_out = tr + 0 * S.tr_w;
+        a.k_trace = tr + 2 * S.tr_w;
+        a.v_trace = tr + 3 * S.tr_w;
+      }
+      if (M.tp > 1 && l > 0) {
+        a.x = S.h2.as<float>();
+        a.x2 = S.dpart.as<float>();
+        a.x_sum_out = S.h.as<float>();
+        launch_gemv<WL_TILED, PRO_NORM_RES, EPI_QKV>(a, S.stream, pdl);
+      } else {
+        a.x = S.h.as<float>();
+        launch_gemv<WL_TILED, PRO_NORM, EPI_QKV>(a, S.stream, pdl);
+      }
+      if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 1 * S.tr_w, S.q.p, nq * 4, cudaMemcpyDeviceToDevice, S.stream));
+    }
+    // attention
+    {
+      AttnArgs a = {};
+      a.q = S.q.as<float>();
+      a.k = S.kcache.as<__half>() + l * layer_cache;
+      a.v = S.vcache.as<__half>() + l * layer_cache;
+      a.ctx = S.ctx.as<float>();
+      a.part = S.attn_part.as<float>();
+      a.counters = S.attn_counters.as<int32_t>();
+      a.st = st;
+      a.n_heads = M.Hl;
+      a.n_kv_heads = M.Hkvl;
+      a.head_dim = hd;
+      a.max_splits = S.max_splits;
+      a.scale = 1.0f / sqrtf((float)hd);
+      const dim3 grid(M.Hkvl, S.max_splits);
+      if (hd == 128)
+        launch_pdl(attention_decode_kernel<128>, grid, dim3(kAttnThreads), 0, S.stream, pdl, a);
+      else
+        launch_pdl(attention_decode_kernel<64>, grid, dim3(kAttnThreads), 0, S.stream, pdl, a);
+      if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 4 * S.tr_w, S.ctx.p, nq * 4, cudaMemcpyDeviceToDevice, S.stream));
+    }
+    // O projection (+ residual)
+    {
+      GemvArgs a = L.o.args();
+      a.x = S.ctx.as<float>();
+      if (M.tp > 1) {
+        a.out = S.opart.as<float>();
+        launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, S.stream, pdl);
+        FABER_NCCL(ncclAllReduce(S.opart.p, S.opart.p, d, ncclFloat32, ncclSum, M.comm, S.stream));
+      } else {
+        a.out = S.h2.as<float>();
+        a.res = S.h.as<float>();
+        launch_gemv<WL_TILED, PRO_PLAIN, EPI_RESID>(a, S.stream, pdl);
+      }
+    }
+    // gate/up + SwiGLU
+    {
+      GemvArgs a = L.gateup.args();
+      a.norm_w = L.ffn_norm.as<float>();
+      a.eps = c.rms_eps;
+      a.out = S.hh.as<float>();
+      if (M.tp > 1) {
+        a.x = S.h.as<float>();
+        a.x2 = S.opart.as<float>();
+        a.x_sum_out = S.h2.as<float>();
+        launch_gemv<WL_TILED, PRO_NORM_RES, EPI_SWIGLU>(a, S.stream, pdl && !M.comm);
+      } else {
+        a.x = S.h2.as<float>();
+        launch_gemv<WL_TILED, PRO_NORM, EPI_SWIGLU>(a, S.stream, pdl);
+      }
+      if (tr) {
+        FABER_CUDA(cudaMemcpyAsync(tr + 5 * S.tr_w, S.h2.p, (size_t)d * 4, cudaMemcpyDeviceToDevice, S.stream));
+        FABER_CUDA(cudaMemcpyAsync(tr + 6 * S.tr_w, S.hh.p, (size_t)M.Fl * 4, cudaMemcpyDeviceToDevice, S.stream));
+      }
+    }
+    // down (+ residual)
+    {
+      GemvArgs a = L.down.args();
+      a.x = S.hh.as<float>();
+      if (M.tp > 1) {
+        a.out = S.dpart.as<float>();
+        launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, S.stream, pdl);
+        FABER_NCCL(ncclAllReduce(S.dpart.p, S.dpart.p, d, ncclFloat32, ncclSum, M.comm, S.stream));
+      } else {
+        a.out = S.h.as<float>();
+        a.res = S.h2.as<float>();
+        launch_gemv<WL_TILED, PRO_PLAIN, EPI_RESID>(a, S.stream, pdl);
+        if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 7 * S.tr_w, S.h.p, (size_t)d * 4, cudaMemcpyDeviceToDevice, S.stream));
+      }
+    }
+  }
+}
+
+// Enqueue the logits step: head GEMV (+argmax) and finalize.
+inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>& eog) {
+  ModelState& M = S.m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  StepState* st = st_ptr(S);
+  GemvArgs a = {};
+  if (c.tied_head) {
+    a.w = M.embd_f16.as<uint8_t>() + (size_t)M.v0 * c.d_model * 2;
+    a.n_rows = M.Vl;
+    a.n_cols = (int)c.d_model;
+    a.nb = (int)c.d_model / 256;
+    a.n_tiles = (M.Vl + kTileRows - 1) / kTileRows;
+  } else {
+    a = M.head.args();
+  }
+  a.norm_w = M.out_norm.as<float>();
+  a.eps = c.rms_eps;
+  a.out = S.logits.as<float>();
+  a.argmax_key = &st->argmax_key;
+  a.finite_flag = &st->finite;
+  a.row_offset = M.v0;
+  a.n_eog = (int)eog.size();
+  for (size_t i = 0; i < eog.size(); ++i) a.eog[i] = eog[i];
+  const bool res = M.tp > 1;
+  if (res) {
+    a.x = S.h2.as<float>();
+    a.x2 = S.dpart.as<float>();
+    a.x_sum_out = S.h.as<float>();
+  } else {
+    a.x = S.h.as<float>();
+  }
+  if (c.tied_head) {
+    if (res) launch_gemv<WL_F16, PRO_NORM_RES, EPI_LOGITS>(a, S.stream, pdl);
+    else launch_gemv<WL_F16, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
+  } else {
+    if (res) launch_gemv<WL_TILED, PRO_NORM_RES, EPI_LOGITS>(a, S.stream, pdl);
+    else launch_gemv<WL_TILED, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
+  }
+  if (M.tp > 1) {
+    FABER_NCCL(ncclAllReduce(&st->argmax_key, &st->argmax_key, 1, ncclUint64, ncclMax, M.comm, S.stream));
+    FABER_NCCL(ncclAllReduce(&st->finite, &st->finite, 1, ncclInt32, ncclMin, M.comm, S.stream));
+  }
+  launch_pdl(finalize_kernel, dim3(1), dim3(1), 0, S.stream, pdl && M.tp == 1, st, S.gen.as<int64_t>(),
+             (int32_t)S.max_ctx);
+}
+
+inline cudaGraphExec_t capture(SessionState& S, const std::function<void()>& body) {
+  cudaGraph_t g = nullptr;
+  FABER_CUDA(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    body();
+  } catch (...) {
+    cudaStreamEndCapture(S.stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  FABER_CUDA(cudaStreamEndCapture(S.stream, &g));
+  cudaGraphExec_t e = nullptr;
+  cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+  cudaGraphDestroy(g);
+  FABER_CUDA(err);
+  return e;
+}
+
+inline void ensure_graphs(SessionState& S, const std::vector<int64_t>& eog) {
+  if (S.graphs_valid && eog == S.graph_eog) return;
+  S.destroy_graphs();
+  const bool pdl = true;
+  S.g_push = capture(S, [&] { enqueue_push(S, pdl); });
+  S.g_logits = capture(S, [&] { enqueue_logits(S, pdl, eog); });
+  S.g_step = capture(S, [&] {
+    enqueue_push(S, pdl);
+    enqueue_logits(S, pdl, eog);
+  });
+  S.graph_eog = eog;
+  S.graphs_valid = true;
+}
+
+inline void check_prefix_complete(SessionState& S) {
+  if (!S.prefix_pending) return;
+  for (uint8_t v : S.prefix_layers)
+    FABER_ARG(v, "K/V prefix installed for some layers only");
+  S.prefix_pending = false;
+}
+
+inline void run_push(SessionState& S, const int64_t* tokens, uint64_t count) {
+  ModelState& M = S.m->s;
+  FABER_CUDA(cudaSetDevice(S.device));
+  check_prefix_complete(S);
+  for (uint64_t i = 0; i < count; ++i)
+    FABER_ARG(tokens[i] >= 0 && tokens[i] < (int64_t)M.cfg.vocab,
+              "token " + std::to_string(tokens[i]) + " is outside the vocab [0, " +
+                  std::to_string(M.cfg.vocab) + ")");
+  require(S.n + count <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
+  if (count == 0) return;
+  FABER_CUDA(cudaMemcpyAsync(S.prompt.p, tokens, count * 8, cudaMemcpyHostToDevice, S.stream));
+  if (S.trace) {
+    for (uint64_t i = 0; i < count; ++i) {
+      FABER_CUDA(cudaMemcpyAsync(&st_ptr(S)->input_token, S.prompt.as<int64_t>() + i, 8,
+                                 cudaMemcpyDeviceToDevice, S.stream));
+      enqueue_push(S, false);
+    }
+  } else {
+    ensure_graphs(S, S.graphs_valid ? S.graph_eog : std::vector<int64_t>{});
+    for (uint64_t i = 0; i < count; ++i) {
+      FABER_CUDA(cudaMemcpyAsync(&st_ptr(S)->input_token, S.prompt.as<int64_t>() + i, 8,
+                                 cudaMemcpyDeviceToDevice, S.stream));
+      FABER_CUDA(cudaGraphLaunch(S.g_push, S.stream));
+    }
+  }
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  StepState st;
+  FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+  require(st.status == 0, FABER_STATUS_KERNEL_ERROR, "device-side token check failed");
+  S.n += count;
+}
+
+inline void gather_logits(SessionState& S, float* host, uint64_t cap) {
+  ModelState& M = S.m->s;
+  require(cap >= M.cfg.vocab, FABER_STATUS_IO_ERROR, "logits buffer smaller than the vocab");
+  if (M.tp > 1) {
+    require(M.cfg.vocab % M.tp == 0, FABER_STATUS_UNSUPPORTED, "vocab must split evenly to gather logits");
+    FABER_NCCL(ncclAllGather(S.logits.p, S.logits_full.p, M.Vl, ncclFloat32, M.comm, S.stream));
+    FABER_CUDA(cudaMemcpyAsync(host, S.logits_full.p, (size_t)M.cfg.vocab * 4, cudaMemcpyDeviceToHost, S.stream));
+  } else {
+    FABER_CUDA(cudaMemcpyAsync(host, S.logits.p, (size_t)M.cfg.vocab * 4, cudaMemcpyDeviceToHost, S.stream));
+  }
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+}
+
+inline void run_position_logits(SessionState& S, float* host, uint64_t cap) {
+  FABER_CUDA(cudaSetDevice(S.device));
+  FABER_ARG(S.n > 0, "the session holds no tokens");
+  FABER_ARG(host != nullptr, "null logits buffer");
+  if (S.trace) {
+    enqueue_logits(S, false, {});
+  } else {
+    ensure_graphs(S, S.graphs_valid ? S.graph_eog : std::vector<int64_t>{});
+    // the EOG set only affects the argmax, not the logits
+    FABER_CUDA(cudaGraphLaunch(S.g_logits, S.stream));
+  }
+  gather_logits(S, host, cap);
+}
+
+inline void run_greedy(SessionState& S, uint32_t n_gen, const int64_t* eog, uint32_t n_eog,
+                       int64_t* out, int32_t* all_finite) {
+  ModelState& M = S.m->s;
+  FABER_CUDA(cudaSetDevice(S.device));
+  FABER_ARG(S.n > 0, "greedy decode needs a prompt");
+  FABER_ARG(n_eog <= (uint32_t)kMaxEog, "at most 8 EOG ids");
+  FABER_ARG(out != nullptr || n_gen == 0, "null output");
+  if (n_gen == 0) return;
+  require(S.n + n_gen - 1 <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
+  check_prefix_complete(S);
+  std::vector<int64_t> e(eog, eog + n_eog);
+  // reset the per-run counters
+  StepState st;
+  FABER_CUDA(cudaMemcpyAsync(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost, S.stream));
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  st.gen_count = 0;
+  st.finite = 1;
+  st.argmax_key = 0;
+  FABER_CUDA(cudaMemcpyAsync(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice, S.stream));
+  if (S.trace) {
+    enqueue_logits(S, false, e);
+    for (uint32_t i = 1; i < n_gen; ++i) {
+      enqueue_push(S, false);
+      enqueue_logits(S, false, e);
+    }
+  } else {
+    ensure_graphs(S, e);
+    FABER_CUDA(cudaEventRecord(S.ev0, S.stream));
+    FABER_CUDA(cudaGraphLaunch(S.g_logits, S.stream));
+    for (uint32_t i = 1; i < n_gen; ++i) FABER_CUDA(cudaGraphLaunch(S.g_step, S.stream));
+    FABER_CUDA(cudaEventRecord(S.ev1, S.stream));
+  }
+  FABER_CUDA(cudaMemcpyAsync(out, S.gen.p, (size_t)n_gen * 8, cudaMemcpyDeviceToHost, S.stream));
+  FABER_CUDA(cudaMemcpyAsync(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost, S.stream));
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  if (!S.trace) FABER_CUDA(cudaEventElapsedTime(&S.last_greedy_ms, S.ev0, S.ev1));
+  if (all_finite) *all_finite = st.finite;
+  S.n += n_gen - 1;
+  (void)M;
+}
+
+inline void set_prefix(SessionState& S, uint32_t layer, const float* k, const float* v, uint64_t n) {
+  ModelState& M = S.m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  FABER_CUDA(cudaSetDevice(S.device));
+  FABER_ARG(layer < c.n_layers && k && v, "bad layer or null K/V");
+  FABER_ARG(n > 0 && n < (uint64_t)S.max_ctx, "prefix length must leave room in the context");
+  FABER_ARG(S.n == 0 || S.prefix_pending, "prefix must be installed into an empty session");
+  if (S.prefix_pending) FABER_ARG(n == S.prefix_n, "every layer must get the same prefix length");
+  const uint64_t hd = c.head_dim, kvs_full = (uint64_t)c.n_kv_heads * hd;
+  const uint64_t kvs = (uint64_t)M.Hkvl * hd, off = (uint64_t)M.rank * kvs;
+  std::vector<uint16_t> hk(n * kvs), hv(n * kvs);
+  for (uint64_t p = 0; p < n; ++p)
+    for (uint64_t i = 0; i < kvs; ++i) {
+      hk[p * kvs + i] = host_f32_to_f16(k[p * kvs_full + off + i]);
+      hv[p * kvs + i] = host_f32_to_f16(v[p * kvs_full + off + i]);
+    }
+  const size_t layer_cache = (size_t)S.max_ctx * kvs;
+  FABER_CUDA(cudaMemcpy(S.kcache.as<__half>() + layer * layer_cache, hk.data(), hk.size() * 2, cudaMemcpyHostToDevice));
+  FABER_CUDA(cudaMemcpy(S.vcache.as<__half>() + layer * layer_cache, hv.data(), hv.size() * 2, cudaMemcpyHostToDevice));
+  S.prefix_layers[layer] = 1;
+  S.prefix_pending = true;
+  S.prefix_n = n;
+  S.n = n;
+  StepState st;
+  FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+  st.n = (int32_t)n;
+  FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
+}
+
+}  // namespace faber
+
+// ---------------------------------------------------------------------------
+// extern "C": model + session
+// ---------------------------------------------------------------------------
+extern "C" {
+
+#define FABER_EXPORT __attribute__((visibility("default")))
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1* cfg,
+                                                       FaberGpuModel** out) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_model_create", [&] {
+    FABER_ARG(cfg && out, "null pointer");
+    validate_config(*cfg);
+    auto m = std::make_unique<FaberGpuModel>();
+    ModelState& M = m->s;
+    M.cfg = *cfg;
+    M.tp = (int)cfg->tp_size;
+    M.rank = (int)cfg->tp_rank;
+    FABER_CUDA(cudaGetDevice(&M.device));
+    M.Hl = (int)(cfg->n_heads / cfg->tp_size);
+    M.Hkvl = (int)(cfg->n_kv_heads / cfg->tp_size);
+    if (M.tp == 1) {
+      M.Fl = (int)cfg->ffn;
+      M.f_blk0 = 0;
+      M.f_blk1 = (int)((cfg->ffn + 255) / 256);
+    } else {
+      const int nF = (int)(cfg->ffn / 256);
+      M.f_blk0 = M.rank * nF / M.tp;
+      M.f_blk1 = (M.rank + 1) * nF / M.tp;
+      M.Fl = (M.f_blk1 - M.f_blk0) * 256;
+    }
+    M.v0 = (int)((uint64_t)M.rank * cfg->vocab / M.tp);
+    M.Vl = (int)((uint64_t)(M.rank + 1) * cfg->vocab / M.tp) - M.v0;
+    M.staged.resize(cfg->n_layers);
+    if (M.tp > 1) {
+      ncclUniqueId id;
+      static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+      std::memcpy(&id, cfg->nccl_unique_id, 128);
+      FABER_NCCL(ncclCommInitRank(&M.comm, M.tp, id, M.rank));
+    }
+    *out = m.release();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_set_tensor(FaberGpuModel* m, const char* name,
+                                                           uint32_t type, const void* data,
+                                                           uint64_t nbytes, uint64_t rows,
+                                                           uint64_t cols) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_model_set_tensor", [&] {
+    FABER_ARG(m && name, "null pointer");
+    model_set_tensor(m->s, name, type, data, nbytes, rows, cols);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_finalize(FaberGpuModel* m) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_model_finalize", [&] {
+    FABER_ARG(m, "null model");
+    model_finalize(m->s);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_free(FaberGpuModel* m) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_model_free", [&] {
+    if (m) {
+      cudaSetDevice(m->s.device);
+      delete m;
+    }
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_device_bytes(const FaberGpuModel* m,
+                                                             uint64_t* bytes) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_model_device_bytes", [&] {
+    FABER_ARG(m && bytes, "null pointer");
+    *bytes = m->s.device_bytes;
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_open(FaberGpuModel* m, const FaberKvLayoutV1* kv,
+                                                       FaberGpuSession** out) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_open", [&] {
+    FABER_ARG(m && kv && out, "null pointer");
+    auto s = std::make_unique<FaberGpuSession>();
+    session_open(s->s, m, *kv);
+    *out = s.release();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_close(FaberGpuSession* s) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_close", [&] { delete s; });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_reset(FaberGpuSession* s) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_reset", [&] {
+    FABER_ARG(s, "null session");
+    SessionState& S = s->s;
+    FABER_CUDA(cudaSetDevice(S.device));
+    FABER_CUDA(cudaStreamSynchronize(S.stream));
+    StepState st = {};
+    st.finite = 1;
+    FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
+    S.n = 0;
+    S.prefix_pending = false;
+    std::fill(S.prefix_layers.begin(), S.prefix_layers.end(), 0);
+    S.c_position = 0;
+    S.c_kv_generations = 0;
+    S.c_history.clear();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_len(const FaberGpuSession* s, uint64_t* n) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_len", [&] {
+    FABER_ARG(s && n, "null pointer");
+    *n = s->s.n;
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_push_token(FaberGpuSession* s, int64_t token) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_push_token", [&] {
+    FABER_ARG(s, "null session");
+    run_push(s->s, &token, 1);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_push_tokens(FaberGpuSession* s,
+                                                              const int64_t* tokens, uint64_t n) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_push_tokens", [&] {
+    FABER_ARG(s && (tokens || n == 0), "null pointer");
+    run_push(s->s, tokens, n);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_position_logits(FaberGpuSession* s, float* logits,
+                                                                  uint64_t cap) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_position_logits", [&] {
+    FABER_ARG(s, "null session");
+    run_position_logits(s->s, logits, cap);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_greedy(FaberGpuSession* s, uint32_t n_gen,
+                                                         const int64_t* eog, uint32_t n_eog,
+                                                         int64_t* out_tokens, int32_t* all_finite) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_greedy", [&] {
+    FABER_ARG(s && (eog || n_eog == 0), "null pointer");
+    run_greedy(s->s, n_gen, eog, n_eog, out_tokens, all_finite);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_set_prefix(FaberGpuSession* s, uint32_t layer,
+                                                             const float* k, const float* v,
+                                                             uint64_t n) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_set_prefix", [&] {
+    FABER_ARG(s, "null session");
+    set_prefix(s->s, layer, k, v, n);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_set_trace(FaberGpuSession* s, int32_t on) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_set_trace", [&] {
+    FABER_ARG(s, "null session");
+    SessionState& S = s->s;
+    ModelState& M = S.m->s;
+    FABER_CUDA(cudaSetDevice(S.device));
+    S.trace = on != 0;
+    if (S.trace && !S.tr.p) {
+      S.tr_w = (int)std::max<uint64_t>({M.cfg.d_model, (uint64_t)M.Fl,
+                                        (uint64_t)M.Hl * M.cfg.head_dim});
+      S.tr.alloc((size_t)M.cfg.n_layers * 8 * S.tr_w * 4);
+      FABER_CUDA(cudaMemset(S.tr.p, 0, S.tr.n));
+    }
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_trace(FaberGpuSession* s, uint32_t layer,
+                                                        uint32_t which, float* out, uint64_t cap,
+                                                        uint64_t* n) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_trace", [&] {
+    FABER_ARG(s && out && n, "null pointer");
+    SessionState& S = s->s;
+    ModelState& M = S.m->s;
+    FABER_ARG(S.trace && S.tr.p, "tracing is off");
+    FABER_ARG(layer < M.cfg.n_layers && which < 8, "bad trace index");
+    const uint64_t hd = M.cfg.head_dim;
+    const uint64_t sizes[8] = {M.cfg.d_model, (uint64_t)M.Hl * hd, (uint64_t)M.Hkvl * hd,
+                               (uint64_t)M.Hkvl * hd, (uint64_t)M.Hl * hd, M.cfg.d_model,
+                               (uint64_t)M.Fl, M.cfg.d_model};
+    const uint64_t cnt = sizes[which];
+    require(cap >= cnt, FABER_STATUS_IO_ERROR, "trace buffer too small");
+    FABER_CUDA(cudaSetDevice(S.device));
+    FABER_CUDA(cudaStreamSynchronize(S.stream));
+    FABER_CUDA(cudaMemcpy(out, S.tr.as<float>() + ((size_t)layer * 8 + which) * S.tr_w, cnt * 4,
+                          cudaMemcpyDeviceToHost));
+    *n = cnt;
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_last_greedy_ms(const FaberGpuSession* s,
+                                                                 float* ms) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_last_greedy_ms", [&] {
+    FABER_ARG(s && ms, "null pointer");
+    *ms = s->s.last_greedy_ms;
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_commit(FaberGpuSession* s, int64_t token,
+                                                         uint32_t position, uint64_t kv_generation,
+                                                         uint64_t publication_boundary,
+                                                         int32_t* outcome) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_commit", [&] {
+    FABER_ARG(s && outcome, "null pointer");
+    SessionState& S = s->s;
+    // SequenceState::commit (src/session.rs:422-456), in its order.
+    FABER_ARG(publication_boundary != 0, "no publication boundary: nothing publishes");
+    if (!S.c_history.empty() && position + 1 == S.c_position &&
+        kv_generation == S.c_kv_generations && S.c_history.back() == token) {
+      *outcome = 1;  // idempotent replay
+      return;
+    }
+    FABER_ARG(position == S.c_position, "out-of-order position: expected " +
+                                            std::to_string(S.c_position) + ", attempted " +
+                                            std::to_string(position));
+    FABER_ARG(kv_generation == S.c_kv_generations + 1,
+              "KV generation gap: expected " + std::to_string(S.c_kv_generations + 1) +
+                  ", attempted " + std::to_string(kv_generation));
+    S.c_history.push_back(token);
+    S.c_position += 1;
+    S.c_kv_generations += 1;
+    *outcome = 0;
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_nccl_unique_id(uint8_t out[128]) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_nccl_unique_id", [&] {
+    FABER_ARG(out, "null pointer");
+    ncclUniqueId id;
+    FABER_NCCL(ncclGetUniqueId(&id));
+    std::memcpy(out, &id, 128);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,406 @@
+// faber_gpu.cu — the C ABI of the B200 Q4_K decoder path (library entry).
+//
+// Single translation unit: the kernels (gemv.cuh, ops.cuh), the host-side
+// repack (repack.hpp), the model/session engine (engine.cuh) and the
+// extern "C" entry points declared in include/faber_gpu.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "abi.hpp"
+#include "gemv.cuh"
+#include "ops.cuh"
+#include "repack.hpp"
+
+namespace faber {
+
+// ---------------------------------------------------------------------------
+// Device facts
+// ---------------------------------------------------------------------------
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+};
+
+inline DeviceInfo device_info() {
+  static std::mutex mu;
+  static std::map<int, DeviceInfo> cache;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  cudaDeviceProp p;
+  FABER_CUDA(cudaGetDeviceProperties(&p, dev));
+  DeviceInfo d{p.multiProcessorCount, p.major, p.minor};
+  cache[dev] = d;
+  return d;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------------------
+// GEMV launch
+// ---------------------------------------------------------------------------
+template <int WL, int PRO, int EPI>
+void launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  auto kern = gemv_kernel<WL, PRO, EPI>;
+  // per device: attribute set once; occupancy cached per shared-memory size
+  static thread_local std::map<int, std::map<size_t, int>> occ_cache;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  auto& per_dev = occ_cache[dev];
+  if (per_dev.empty())
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+  const size_t smem = gemv_smem_bytes(a.nb);
+  require(smem <= 232448, FABER_STATUS_UNSUPPORTED, "GEMV input too long for shared-memory staging");
+  int occ = 0;
+  auto it = per_dev.find(smem);
+  if (it == per_dev.end()) {
+    FABER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGemvThreads, smem));
+    per_dev[smem] = occ;
+  } else {
+    occ = it->second;
+  }
+  occ = std::max(1, occ);
+  const int grid = std::max(1, std::min(a.n_tiles, occ * device_info().sms));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  FABER_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+template <class K, class... Args>
+void launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  FABER_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
+}
+
+// ---------------------------------------------------------------------------
+// Device buffers
+// ---------------------------------------------------------------------------
+struct DevBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  int dev = -1;
+  DevBuf() = default;
+  explicit DevBuf(size_t bytes) { alloc(bytes); }
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n), dev(o.dev) { o.p = nullptr; o.n = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) { release(); p = o.p; n = o.n; dev = o.dev; o.p = nullptr; o.n = 0; }
+    return *this;
+  }
+  ~DevBuf() { release(); }
+  void alloc(size_t bytes) {
+    release();
+    FABER_CUDA(cudaGetDevice(&dev));
+    if (bytes) {
+      cudaError_t e = cudaMalloc(&p, bytes);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        throw Error(FABER_STATUS_ALLOCATION, "cudaMalloc(" + std::to_string(bytes) + ") failed: " +
+                                                 cudaGetErrorString(e));
+      }
+    }
+    n = bytes;
+  }
+  void release() {
+    if (p) {
+      int cur = -1;
+      cudaGetDevice(&cur);
+      if (dev >= 0 && cur != dev) cudaSetDevice(dev);
+      cudaFree(p);
+      if (dev >= 0 && cur != dev && cur >= 0) cudaSetDevice(cur);
+    }
+    p = nullptr;
+    n = 0;
+  }
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+inline void upload(DevBuf& b, const void* host, size_t bytes) {
+  b.alloc(bytes);
+  if (bytes) FABER_CUDA(cudaMemcpy(b.p, host, bytes, cudaMemcpyHostToDevice));
+}
+
+// A Q4_K weight in tile layout on the device.
+struct DeviceTiled {
+  DevBuf w, xoff, rowmap;
+  int n_tiles = 0, nb = 0, rows = 0, cols = 0;
+  bool identity = true;
+  uint64_t hash = 0;
+  void from(const TiledQ4k& T) {
+    upload(w, T.data.data(), T.data.size());
+    n_tiles = T.n_tiles;
+    nb = T.nb;
+    rows = T.rows;
+    cols = T.cols;
+    identity = T.identity;
+    hash = repack_hash(T);
+    if (!identity) {
+      upload(xoff, T.xoff.data(), T.xoff.size() * sizeof(int32_t));
+      upload(rowmap, T.rowmap.data(), T.rowmap.size() * sizeof(int32_t));
+    } else {
+      xoff.release();
+      rowmap.release();
+    }
+  }
+  GemvArgs args() const {
+    GemvArgs a = {};
+    a.w = w.as<uint8_t>();
+    a.n_tiles = n_tiles;
+    a.nb = nb;
+    a.n_rows = rows;
+    a.n_cols = cols;
+    a.tile_xoff = identity ? nullptr : xoff.as<int32_t>();
+    a.row_map = identity ? nullptr : rowmap.as<int32_t>();
+    return a;
+  }
+};
+
+}  // namespace faber
+
+struct FaberGpuQ4kTensor {
+  faber::DeviceTiled t;
+};
+
+#include "engine.cuh"
+
+using namespace faber;
+
+// ---------------------------------------------------------------------------
+// extern "C" entry points
+// ---------------------------------------------------------------------------
+extern "C" {
+
+__attribute__((visibility("default"))) uint32_t faber_gpu_v2_abi_version(void) { return 2; }
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_last_error(char* buf,
+                                                                              uint64_t cap) {
+  if (!buf || cap == 0) return status(FABER_STATUS_INVALID_ARGUMENT);
+  const size_t n = std::min<size_t>(cap - 1, g_last_error.size());
+  std::memcpy(buf, g_last_error.data(), n);
+  buf[n] = 0;
+  return status(FABER_STATUS_OK);
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_init(int32_t device) {
+  return guarded("faber_gpu_v2_init", [&] {
+    int count = 0;
+    FABER_CUDA(cudaGetDeviceCount(&count));
+    FABER_ARG(device >= 0 && device < count, "device ordinal out of range");
+    FABER_CUDA(cudaSetDevice(device));
+    const DeviceInfo d = device_info();
+    require(d.major == 10, FABER_STATUS_UNSUPPORTED,
+            "this library is built for sm_100a (B200); device is sm_" +
+                std::to_string(d.major * 10 + d.minor));
+    FABER_CUDA(cudaFree(nullptr));
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_fault_inject(
+    const char* entry, int32_t code, uint32_t count) {
+  if (!entry) return status(FABER_STATUS_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> lk(g_faults.mu);
+  if (count == 0) g_faults.table.erase(entry);
+  else g_faults.table[entry] = {code, count};
+  return status(FABER_STATUS_OK);
+}
+
+// --- placement ABI (hosts/llvm/src/gpu_placement.rs:53-137) --------------
+namespace {
+std::mutex g_place_mu;
+std::map<uint64_t, DevBuf>& placed() {
+  static std::map<uint64_t, DevBuf> m;
+  return m;
+}
+}  // namespace
+
+__attribute__((visibility("default"))) FaberRtStatusV1 __faber_gpu_v1_copy_in(
+    uint64_t logical_id, const uint8_t* data_ptr, uint64_t data_len, uint32_t dtype) {
+  (void)dtype;
+  return guarded("__faber_gpu_v1_copy_in", [&] {
+    FABER_ARG(!(data_len > 0 && data_ptr == nullptr), "null data pointer with nonzero length");
+    std::lock_guard<std::mutex> lk(g_place_mu);
+    DevBuf b;
+    upload(b, data_ptr, data_len);
+    placed()[logical_id] = std::move(b);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 __faber_gpu_v1_readback(
+    uint64_t logical_id, uint8_t* dest_ptr, uint64_t dest_capacity, uint64_t* actual_len) {
+  return guarded("__faber_gpu_v1_readback", [&] {
+    FABER_ARG(dest_ptr != nullptr && actual_len != nullptr, "null destination");
+    std::lock_guard<std::mutex> lk(g_place_mu);
+    auto it = placed().find(logical_id);
+    FABER_ARG(it != placed().end(), "unknown logical buffer id");
+    require(it->second.n <= dest_capacity, FABER_STATUS_IO_ERROR, "destination capacity too small");
+    if (it->second.n) FABER_CUDA(cudaMemcpy(dest_ptr, it->second.p, it->second.n, cudaMemcpyDeviceToHost));
+    *actual_len = it->second.n;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 __faber_gpu_v1_sync(uint64_t logical_id) {
+  (void)logical_id;
+  return guarded("__faber_gpu_v1_sync", [&] { FABER_CUDA(cudaDeviceSynchronize()); });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_buffer_device_ptr(
+    uint64_t logical_id, void** dev_ptr, uint64_t* len) {
+  return guarded("faber_gpu_v2_buffer_device_ptr", [&] {
+    FABER_ARG(dev_ptr && len, "null output");
+    std::lock_guard<std::mutex> lk(g_place_mu);
+    auto it = placed().find(logical_id);
+    FABER_ARG(it != placed().end(), "unknown logical buffer id");
+    *dev_ptr = it->second.p;
+    *len = it->second.n;
+  });
+}
+
+// --- stateless kernels ------------------------------------------------------
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_dequant_q4k(
+    const uint8_t* blocks, uint64_t n_blocks, float* out, int32_t f16_round, void* stream) {
+  return guarded("faber_gpu_v2_dequant_q4k", [&] {
+    FABER_ARG(n_blocks == 0 || (blocks && out), "null pointer");
+    if (n_blocks == 0) return;
+    const uint64_t threads = n_blocks * 32;
+    dequant_q4k_native_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+        blocks, n_blocks, out, f16_round ? 1 : 0);
+    FABER_CUDA(cudaGetLastError());
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_f16_round(const float* x,
+                                                                             float* y, uint64_t n,
+                                                                             void* stream) {
+  return guarded("faber_gpu_v2_f16_round", [&] {
+    FABER_ARG(n == 0 || (x && y), "null pointer");
+    if (n == 0) return;
+    const unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256, 4 * 148 * 8);
+    f16_round_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, y, n);
+    FABER_CUDA(cudaGetLastError());
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gemv_q4k(
+    const uint8_t* w_blocks, uint64_t rows, uint64_t cols, const float* x, float* y,
+    void* stream) {
+  return guarded("faber_gpu_v2_gemv_q4k", [&] {
+    FABER_ARG(rows > 0 && cols > 0 && w_blocks && x && y, "null pointer or empty shape");
+    require(cols % 256 == 0, FABER_STATUS_UNSUPPORTED,
+            "native-layout GEMV needs cols % 256 == 0; upload with faber_gpu_v2_q4k_upload");
+    FABER_ARG(rows < (1u << 30) && cols < (1u << 20), "shape too large");
+    GemvArgs a = {};
+    a.w = w_blocks;
+    a.n_rows = (int)rows;
+    a.n_cols = (int)cols;
+    a.nb = (int)(cols / 256);
+    a.n_tiles = (int)((rows + kTileRows - 1) / kTileRows);
+    a.x = x;
+    a.out = y;
+    launch_gemv<WL_NATIVE, PRO_PLAIN, EPI_STORE>(a, as_stream(stream), false);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_upload(
+    const uint8_t* host_blocks, uint64_t nbytes, uint64_t rows, uint64_t cols,
+    FaberGpuQ4kTensor** out) {
+  return guarded("faber_gpu_v2_q4k_upload", [&] {
+    FABER_ARG(out && host_blocks && rows > 0 && cols > 0, "null pointer or empty shape");
+    FABER_ARG(rows < (1u << 30) && cols < (1u << 20), "shape too large");
+    FABER_ARG((rows * cols) % 256 == 0, "element count is not a multiple of the Q4_K block");
+    const uint64_t nblocks = rows * cols / 256;
+    FABER_ARG(nbytes == nblocks * kQ4kBlockBytes,
+              "packed tensor is " + std::to_string(nbytes) + " bytes, expected exactly " +
+                  std::to_string(nblocks * kQ4kBlockBytes));
+    TiledQ4k T = repack_q4k((int)rows, (int)cols, [&](int j) {
+      return RowSeg{host_blocks, nblocks, (uint64_t)j * cols};
+    });
+    auto t = std::make_unique<FaberGpuQ4kTensor>();
+    t->t.from(T);
+    *out = t.release();
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_free(FaberGpuQ4kTensor* t) {
+  return guarded("faber_gpu_v2_q4k_free", [&] { delete t; });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_gemv(
+    const FaberGpuQ4kTensor* t, const float* x, float* y, void* stream) {
+  return guarded("faber_gpu_v2_q4k_gemv", [&] {
+    FABER_ARG(t && x && y, "null pointer");
+    GemvArgs a = t->t.args();
+    a.x = x;
+    a.out = y;
+    launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, as_stream(stream), false);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_dequant_rows(
+    const FaberGpuQ4kTensor* t, float* out, int32_t f16_round, void* stream) {
+  return guarded("faber_gpu_v2_q4k_dequant_rows", [&] {
+    FABER_ARG(t && out, "null pointer");
+    const DeviceTiled& d = t->t;
+    const uint64_t warps = (uint64_t)d.n_tiles * kTileRows * d.nb;
+    dequant_q4k_tiled_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, as_stream(stream)>>>(
+        d.w.as<uint8_t>(), d.n_tiles, d.nb, d.rows, d.cols,
+        d.identity ? nullptr : d.xoff.as<int32_t>(), d.identity ? nullptr : d.rowmap.as<int32_t>(),
+        out, f16_round ? 1 : 0);
+    FABER_CUDA(cudaGetLastError());
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_repack_hash(
+    const FaberGpuQ4kTensor* t, uint64_t* hash) {
+  return guarded("faber_gpu_v2_q4k_repack_hash", [&] {
+    FABER_ARG(t && hash, "null pointer");
+    *hash = t->t.hash;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_kv_layout_bytes(
+    const FaberKvLayoutV1* l, uint64_t* total, uint64_t* admitted) {
+  return guarded("faber_gpu_v2_kv_layout_bytes", [&] {
+    FABER_ARG(l && total && admitted, "null pointer");
+    FABER_ARG(l->slots && l->context_length && l->layer_count && l->kv_head_count && l->head_dim,
+              "a zero-sized KV layout is not a layout");
+    FABER_ARG(l->dtype <= 1, "unknown KV dtype");
+    const unsigned __int128 per_layer =
+        (unsigned __int128)l->context_length * l->kv_head_count * l->head_dim;
+    const unsigned __int128 elems = per_layer * l->layer_count * 2u;
+    const unsigned __int128 bytes = elems * (l->dtype == 0 ? 4u : 2u) * l->slots;
+    require(bytes <= (unsigned __int128)UINT64_MAX, FABER_STATUS_IO_ERROR, "KV byte count overflows");
+    require(bytes + l->reserve_bytes <= (unsigned __int128)UINT64_MAX, FABER_STATUS_IO_ERROR,
+            "KV admitted byte count overflows");
+    *total = (uint64_t)bytes;
+    *admitted = (uint64_t)(bytes + l->reserve_bytes);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,271 @@
+/* faber_gpu.h — C ABI of the B200 (sm_100a) Q4_K decoder path.
+ *
+ * Every entry point returns FaberRtStatusV1 by value, never throws or
+ * unwinds across the boundary, and takes plain pointers and sizes (no torch
+ * or C++ types). Status conventions follow faber-runtime's host ABI
+ * (src/host_abi.rs:313-323, 378-389): OK 0, INVALID_ARGUMENT 1, IO_ERROR 2,
+ * PANIC 3 (an internal C++ exception, the analogue of catch_unwind ->
+ * STATUS_PANIC in hosts/llvm/src/gpu_placement.rs:29-31), UNSUPPORTED 4,
+ * FALLIBLE 5. Codes >= 16 are the device-runtime failures named by the
+ * reference's backend error taxonomy
+ * (src/execution_transaction/backend.rs:17-54). The message of the last
+ * failure on the calling thread is available from faber_gpu_v2_last_error.
+ *
+ * Threading: one process may drive several devices; calls on one model or
+ * session must be serialized by the caller (the reference's per-session
+ * rule, src/session.rs:625). The placement ABI (v1 symbols) is guarded by
+ * one process-wide mutex like hosts/llvm/src/gpu_placement.rs:27.
+ */
+#ifndef FABER_GPU_H
+#define FABER_GPU_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct FaberRtStatusV1 {
+  int32_t code;
+} FaberRtStatusV1;
+
+enum {
+  FABER_STATUS_OK = 0,
+  FABER_STATUS_INVALID_ARGUMENT = 1,
+  FABER_STATUS_IO_ERROR = 2,
+  FABER_STATUS_PANIC = 3,
+  FABER_STATUS_UNSUPPORTED = 4,
+  FABER_STATUS_FALLIBLE = 5,
+  FABER_STATUS_TIMEOUT = 16,
+  FABER_STATUS_DEVICE_LOSS = 17,
+  FABER_STATUS_CANCELLED = 18,
+  FABER_STATUS_ALLOCATION = 19,
+  FABER_STATUS_CUDA_ERROR = 20,
+  FABER_STATUS_KERNEL_ERROR = 21
+};
+
+/* GGUF dtype ids of the admitted tensor types (src/gguf.rs:135-144). */
+enum {
+  FABER_GGML_F32 = 0,
+  FABER_GGML_Q5_0 = 6,
+  FABER_GGML_Q8_0 = 8,
+  FABER_GGML_Q4_K = 12,
+  FABER_GGML_Q6_K = 14
+};
+
+typedef struct FaberGpuModel FaberGpuModel;
+typedef struct FaberGpuSession FaberGpuSession;
+
+/* ------------------------------------------------------------------------
+ * Library / diagnostics
+ * ------------------------------------------------------------------------ */
+
+/* ABI version of this header (2). */
+uint32_t faber_gpu_v2_abi_version(void);
+
+/* Copy the last failure message of the calling thread (NUL-terminated,
+ * truncated to cap). */
+FaberRtStatusV1 faber_gpu_v2_last_error(char* buf, uint64_t cap);
+
+/* Select the CUDA device for subsequent calls on this thread and check that
+ * it is an sm_100 part. */
+FaberRtStatusV1 faber_gpu_v2_init(int32_t device_ordinal);
+
+/* Host-side fault table (test support): the next `count` calls to the entry
+ * point named `entry` fail with `status` before any device work is issued,
+ * mirroring the fault classes of src/fake_device.rs:44-75. count 0 clears. */
+FaberRtStatusV1 faber_gpu_v2_fault_inject(const char* entry, int32_t status, uint32_t count);
+
+/* ------------------------------------------------------------------------
+ * Placement ABI — replaces hosts/llvm/src/gpu_placement.rs:53-137
+ * (__faber_gpu_v1_copy_in / readback / sync), now backed by device memory on
+ * the current device. Same argument meaning and error behaviour: a null
+ * pointer with a nonzero length is INVALID_ARGUMENT, an unknown id is
+ * INVALID_ARGUMENT, a too-small destination is IO_ERROR, copy_in replaces an
+ * existing buffer.
+ * ------------------------------------------------------------------------ */
+FaberRtStatusV1 __faber_gpu_v1_copy_in(uint64_t logical_id, const uint8_t* data_ptr,
+                                       uint64_t data_len, uint32_t dtype);
+FaberRtStatusV1 __faber_gpu_v1_readback(uint64_t logical_id, uint8_t* dest_ptr,
+                                        uint64_t dest_capacity, uint64_t* actual_len);
+FaberRtStatusV1 __faber_gpu_v1_sync(uint64_t logical_id);
+/* Device address and length of a placed buffer (for the kernels below). */
+FaberRtStatusV1 faber_gpu_v2_buffer_device_ptr(uint64_t logical_id, void** dev_ptr,
+                                               uint64_t* len);
+
+/* ------------------------------------------------------------------------
+ * Stateless kernels on device pointers. `stream` is a cudaStream_t (NULL:
+ * the legacy default stream). All are asynchronous.
+ * ------------------------------------------------------------------------ */
+
+/* dequant_row for Q4_K — src/dequant.rs:194-217 via :323-340: n_blocks
+ * native 144-byte super-blocks -> 256*n_blocks f32. f16_round != 0 applies
+ * the oracle's weight rounding f32->f16(RN)->f32 (src/cpu_oracle.rs:356-360).
+ * Bit-exact with the reference. */
+FaberRtStatusV1 faber_gpu_v2_dequant_q4k(const uint8_t* blocks, uint64_t n_blocks, float* out,
+                                         int32_t f16_round, void* stream);
+
+/* f32 -> f16 (round-to-nearest-even) -> f32, element-wise: kv_f16_round
+ * (src/cpu_oracle.rs:225-294). */
+FaberRtStatusV1 faber_gpu_v2_f16_round(const float* x, float* y, uint64_t n, void* stream);
+
+/* dense over a Q4_K weight — src/decoder_ops.rs:378-406 applied to the
+ * f16-rounded dequantized weight (src/cpu_oracle.rs:302-360):
+ * y[j] = sum_i w[j][i] * x[i], w given as rows*cols/256 native super-blocks
+ * in GGUF order (row j = elements [j*cols, (j+1)*cols) of the flat tensor;
+ * cols must be a multiple of 32). The weight is repacked into the kernel's
+ * tile layout on every call (a scratch allocation); the model API uploads
+ * once instead. */
+FaberRtStatusV1 faber_gpu_v2_gemv_q4k(const uint8_t* w_blocks, uint64_t rows, uint64_t cols,
+                                      const float* x, float* y, void* stream);
+
+/* A Q4_K weight resident on the device in the repacked tile layout
+ * (the reference's Declared repack identity, src/quantized_tensor_layout.rs:
+ * 269-278,483-487). Created from native GGUF bytes on the host. */
+typedef struct FaberGpuQ4kTensor FaberGpuQ4kTensor;
+FaberRtStatusV1 faber_gpu_v2_q4k_upload(const uint8_t* host_blocks, uint64_t nbytes,
+                                        uint64_t rows, uint64_t cols, FaberGpuQ4kTensor** out);
+FaberRtStatusV1 faber_gpu_v2_q4k_free(FaberGpuQ4kTensor* t);
+/* y = dense(w, x) with the resident weight (x, y device pointers). */
+FaberRtStatusV1 faber_gpu_v2_q4k_gemv(const FaberGpuQ4kTensor* t, const float* x, float* y,
+                                      void* stream);
+/* Dequantize the resident (repacked) weight back to [rows][cols] f32 —
+ * proves the repack is value-identical to dequant_tensor. */
+FaberRtStatusV1 faber_gpu_v2_q4k_dequant_rows(const FaberGpuQ4kTensor* t, float* out,
+                                              int32_t f16_round, void* stream);
+/* Repack identity (a 64-bit hash of the layout parameters and source bytes). */
+FaberRtStatusV1 faber_gpu_v2_q4k_repack_hash(const FaberGpuQ4kTensor* t, uint64_t* hash);
+
+/* ------------------------------------------------------------------------
+ * Model + session — the device analogue of CpuOracle / ForwardRun /
+ * run_greedy (src/cpu_oracle.rs:409-445, 808-926; src/greedy_run.rs:186-248)
+ * under the session contract of src/session.rs and the KV layout of
+ * src/kv_cache.rs.
+ * ------------------------------------------------------------------------ */
+
+typedef struct FaberModelConfigV1 {
+  uint32_t n_layers;
+  uint32_t d_model;
+  uint32_t n_heads;
+  uint32_t n_kv_heads;
+  uint32_t head_dim;
+  uint32_t ffn;
+  uint32_t vocab;
+  uint32_t tied_head; /* 1: logits use token_embd (no output.weight) */
+  float rms_eps;
+  float rope_theta;
+  /* tensor parallelism: this process is rank tp_rank of tp_size. tp_size 1
+   * is single-GPU. For tp_size > 1, nccl_unique_id holds the 128-byte
+   * ncclUniqueId shared by the group. */
+  uint32_t tp_size;
+  uint32_t tp_rank;
+  uint8_t nccl_unique_id[128];
+} FaberModelConfigV1;
+
+/* KvCacheLayout — src/kv_cache.rs:504-626. dtype 0 = f32 (the reference's
+ * only admitted dtype), 1 = f16 (value-identical: every cached K/V is an
+ * f16-rounded value, src/cpu_oracle.rs:598-601). */
+typedef struct FaberKvLayoutV1 {
+  uint32_t slots;
+  uint32_t context_length;
+  uint32_t layer_count;
+  uint32_t kv_head_count;
+  uint32_t head_dim;
+  uint32_t dtype;
+  uint64_t reserve_bytes;
+} FaberKvLayoutV1;
+
+/* Storage and admitted bytes of a layout (KvCacheLayout::total_bytes /
+ * admitted_bytes, src/kv_cache.rs:605-626). A zero dimension is
+ * INVALID_ARGUMENT (KvCacheLayout::new returns None), overflow is IO_ERROR. */
+FaberRtStatusV1 faber_gpu_v2_kv_layout_bytes(const FaberKvLayoutV1* layout, uint64_t* total,
+                                             uint64_t* admitted);
+
+FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1* cfg, FaberGpuModel** out);
+/* Upload one tensor by its GGUF name (token_embd.weight, output_norm.weight,
+ * output.weight, blk.N.{attn_norm,attn_q,attn_k,attn_v,attn_output,ffn_norm,
+ * ffn_gate,ffn_up,ffn_down}.weight). rows = out_features, cols =
+ * in_features (1 for vectors). The byte count must be exactly the packed
+ * size (src/dequant.rs:323-333, RowBytesMismatch -> INVALID_ARGUMENT). With
+ * tp_size > 1 every rank passes the full tensor and keeps its shard. */
+FaberRtStatusV1 faber_gpu_v2_model_set_tensor(FaberGpuModel* m, const char* name,
+                                              uint32_t ggml_type, const void* host_data,
+                                              uint64_t nbytes, uint64_t rows, uint64_t cols);
+/* Check coverage (every tensor present, src/cpu_oracle.rs:409-445) and
+ * build the per-model device state. */
+FaberRtStatusV1 faber_gpu_v2_model_finalize(FaberGpuModel* m);
+FaberRtStatusV1 faber_gpu_v2_model_free(FaberGpuModel* m);
+/* Bytes of weights resident on this device. */
+FaberRtStatusV1 faber_gpu_v2_model_device_bytes(const FaberGpuModel* m, uint64_t* bytes);
+
+FaberRtStatusV1 faber_gpu_v2_session_open(FaberGpuModel* m, const FaberKvLayoutV1* kv,
+                                          FaberGpuSession** out);
+FaberRtStatusV1 faber_gpu_v2_session_close(FaberGpuSession* s);
+/* Forget every position (a new sequence epoch; weights stay resident). */
+FaberRtStatusV1 faber_gpu_v2_session_reset(FaberGpuSession* s);
+FaberRtStatusV1 faber_gpu_v2_session_len(const FaberGpuSession* s, uint64_t* n);
+/* ForwardRun::push_token (src/cpu_oracle.rs:859-912): append one token.
+ * A token outside [0, vocab) or a full context is INVALID_ARGUMENT / IO_ERROR
+ * and leaves the session unchanged. */
+FaberRtStatusV1 faber_gpu_v2_session_push_token(FaberGpuSession* s, int64_t token);
+/* Append n tokens (the prompt) — same as n push_token calls. */
+FaberRtStatusV1 faber_gpu_v2_session_push_tokens(FaberGpuSession* s, const int64_t* tokens,
+                                                 uint64_t n);
+/* ForwardRun::position_logits (src/cpu_oracle.rs:920-926): full-vocab raw
+ * logits at the sequence end into a host buffer of cap floats. */
+FaberRtStatusV1 faber_gpu_v2_session_position_logits(FaberGpuSession* s, float* logits,
+                                                     uint64_t cap);
+/* run_greedy's loop (src/greedy_run.rs:186-248): n_gen steps of
+ * logits -> argmax over non-EOG ids (lowest id wins ties,
+ * src/cpu_oracle.rs:979-995) -> feed back. Tokens go to out_tokens (host);
+ * *all_finite receives the finite gate over every step's logits. The token
+ * stays on the device between steps. */
+FaberRtStatusV1 faber_gpu_v2_session_greedy(FaberGpuSession* s, uint32_t n_gen,
+                                            const int64_t* eog, uint32_t n_eog,
+                                            int64_t* out_tokens, int32_t* all_finite);
+/* Install a K/V prefix of n positions for one layer (host f32 [n][kv_heads*
+ * head_dim]; stored f16-rounded like every cached value). All layers must be
+ * given the same n before the next push. */
+FaberRtStatusV1 faber_gpu_v2_session_set_prefix(FaberGpuSession* s, uint32_t layer,
+                                                const float* k, const float* v, uint64_t n);
+/* Layer intermediates of the last push (test support): which = 0 attn_in,
+ * 1 q_rot, 2 k_rot, 3 v, 4 ctx, 5 h2, 6 hh, 7 h_out; only when the session
+ * was opened with tracing (faber_gpu_v2_session_set_trace). */
+FaberRtStatusV1 faber_gpu_v2_session_set_trace(FaberGpuSession* s, int32_t on);
+FaberRtStatusV1 faber_gpu_v2_session_trace(FaberGpuSession* s, uint32_t layer, uint32_t which,
+                                           float* out, uint64_t cap, uint64_t* n);
+/* Device timing of the last greedy call: milliseconds between the first and
+ * last decode step on the device (CUDA events). */
+FaberRtStatusV1 faber_gpu_v2_session_last_greedy_ms(const FaberGpuSession* s, float* ms);
+
+/* Token commit — SequenceState::commit (src/session.rs:422-456): advances
+ * token/position/kv-generation together; an exact replay of the last commit
+ * is a no-op success (*outcome = 1), out-of-order position or a KV
+ * generation gap is INVALID_ARGUMENT and changes nothing; an empty
+ * publication boundary is INVALID_ARGUMENT. *outcome = 0 when applied. */
+FaberRtStatusV1 faber_gpu_v2_session_commit(FaberGpuSession* s, int64_t token,
+                                            uint32_t position, uint64_t kv_generation,
+                                            uint64_t publication_boundary, int32_t* outcome);
+
+/* ------------------------------------------------------------------------
+ * Seeded synthetic inputs (counter-based splitmix64; identical bytes for
+ * any thread count). stream separates independent tensors.
+ * ------------------------------------------------------------------------ */
+/* Q4_K super-blocks: d, dmin = f16(U[1e-3, 2e-2]); scales[12], qs[128]
+ * uniform bytes (every 6-bit scale/min and 4-bit quant uniform). */
+FaberRtStatusV1 faber_synth_q4k(uint64_t seed, uint64_t stream, uint64_t n_blocks,
+                                uint8_t* out);
+/* f32 N(mean, std) (Box-Muller in double). */
+FaberRtStatusV1 faber_synth_normal_f32(uint64_t seed, uint64_t stream, uint64_t n, float mean,
+                                       float std, float* out);
+/* token ids uniform in [0, vocab). */
+FaberRtStatusV1 faber_synth_tokens(uint64_t seed, uint64_t stream, uint64_t n, uint32_t vocab,
+                                   int64_t* out);
+/* The 128-byte ncclUniqueId for a TP group (rank 0 creates, then shares). */
+FaberRtStatusV1 faber_gpu_v2_nccl_unique_id(uint8_t out[128]);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FABER_GPU_H */

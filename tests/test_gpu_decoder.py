@@ -1,0 +1,173 @@
+"""GPU decoder parity against the CPU oracle (through the C ABI).
+
+* tiny (4 layers, d 512, 8 heads x 64, FFN 1408, vocab 32000, tied head): a
+  32-token prompt then 64 greedy tokens, token-identical to run_greedy, and
+  teacher-forced logits at every step within 1e-3 x RMS;
+* layer-level intermediates of the first pushes (trace mode);
+* the 7B shape (d 4096, 32 heads x 128, FFN 11008, vocab 32000) cut to two
+  layers, over an installed 256-position K/V prefix (the oracle cannot
+  prefill thousands of 7B positions in test time);
+* the 70B shape's GQA (64/8 heads) cut to one layer and 1/8 width is covered
+  by the gqa config below;
+* fail-closed behaviour (empty prompt, out-of-range token, full context) and
+  the token-commit contract of src/session.rs:422-456.
+"""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RMS_TOL = 1e-3
+
+
+def within(gpu, ref, tol=RMS_TOL):
+    gpu = np.asarray(gpu, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rms = np.sqrt(np.mean(ref ** 2))
+    err = np.max(np.abs(gpu - ref))
+    assert np.all(np.isfinite(gpu))
+    assert err <= tol * rms, f"max|err| {err:.3e} > {tol} x RMS {rms:.3e}"
+    return err / rms
+
+
+def build_pair(cfg, seed, norms="ones"):
+    import oracle as o
+    from faber_runtime_b200 import DeviceModel, synth
+    tensors = list(synth.model_tensors(cfg, seed, norms=norms))
+    om = o.OracleModel(cfg, {n: (t, a, r, c) for n, t, a, r, c in tensors})
+    dm = DeviceModel(cfg, tensors)
+    return om, dm, tensors
+
+
+@pytest.fixture(scope="module")
+def tiny(cuda):
+    from faber_runtime_b200 import TINY
+    return build_pair(TINY, 2024)
+
+
+def test_tiny_greedy_token_identical_and_logits_close(tiny):
+    import oracle as o
+    from faber_runtime_b200 import TINY, ForwardRun, run_greedy, synth
+    om, dm, _ = tiny
+    prompt = synth.tokens(2024, 99, 32, TINY.vocab)
+    ref_tokens, ref_logits, ref_finite = om.greedy(prompt, 64, eog=(), want_logits=True)
+    rec = run_greedy(dm, prompt, ref_tokens.tolist())
+    assert rec.all_finite and ref_finite
+    assert rec.generated_tokens == ref_tokens.tolist(), rec.divergence_field()
+    assert rec.divergence_field() == "none"
+    # teacher-forced logits at every step
+    run = ForwardRun(dm, prompt, context_length=128)
+    worst = 0.0
+    for i in range(64):
+        worst = max(worst, within(run.position_logits(), ref_logits[i]))
+        run.push_token(int(ref_tokens[i]))
+    assert worst < 1e-4
+    assert len(run) == 32 + 64
+
+
+def test_tiny_forward_one_matches(tiny):
+    import oracle as o
+    from faber_runtime_b200 import synth
+    om, dm, _ = tiny
+    toks = synth.tokens(7, 7, 9, 32000)
+    r = o.OracleRun(om, 16)
+    for t in toks:
+        r.push_token(int(t))
+    within(dm.forward_one(toks), r.position_logits())
+
+
+def test_tiny_layer_trace(tiny):
+    import oracle as o
+    from faber_runtime_b200 import ForwardRun, synth
+    om, dm, _ = tiny
+    toks = synth.tokens(3, 3, 5, 32000)
+    orun = o.OracleRun(om, 16, trace=True)
+    drun = ForwardRun(dm, context_length=16, trace=True)
+    for i, t in enumerate(toks):
+        orun.push_token(int(t))
+        drun.push_token(int(t))
+        if i == 0:
+            # layer 0 normalizes the exact (f16-rounded) embedding: rms_norm is
+            # reproduced to the bit (f64 sum, IEEE sqrt/div, two rounded muls)
+            a, b = drun.trace(0, "attn_in"), orun.trace(0, "attn_in")
+            ulp = np.abs(a.view(np.int32).astype(np.int64) - b.view(np.int32).astype(np.int64))
+            assert ulp.max() <= 1
+        for layer in range(om.cfg.n_layers):
+            for which in ("attn_in", "q_rot", "k_rot", "v", "ctx", "h2", "hh", "h_out"):
+                within(drun.trace(layer, which), orun.trace(layer, which))
+    within(drun.position_logits(), orun.position_logits())
+
+
+def test_random_norm_weights_gqa_model(cuda):
+    """GQA (16 query heads over 4 kv heads, head_dim 128) with random per-layer
+    norm weights, so the f16 rounding of norms is exercised."""
+    import oracle as o
+    from faber_runtime_b200 import ForwardRun, ModelConfig, synth
+    cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=4, head_dim=128, ffn=2816,
+                      vocab=4096, tied_head=False, rope_theta=500000.0, name="gqa-test")
+    om, dm, _ = build_pair(cfg, 77, norms="random")
+    prompt = synth.tokens(77, 1, 12, cfg.vocab)
+    ref_tokens, ref_logits, _ = om.greedy(prompt, 12, want_logits=True)
+    run = ForwardRun(dm, prompt, context_length=64)
+    toks, fin = run.greedy(12)
+    assert fin and toks.tolist() == ref_tokens.tolist()
+    run2 = ForwardRun(dm, prompt, context_length=64)
+    for i in range(12):
+        within(run2.position_logits(), ref_logits[i])
+        run2.push_token(int(ref_tokens[i]))
+
+
+def test_7b_shape_two_layers_over_prefix(cuda):
+    import oracle as o
+    from faber_runtime_b200 import LLAMA2_7B, ForwardRun, synth
+    cfg = LLAMA2_7B.with_layers(2)
+    om, dm, _ = build_pair(cfg, 7)
+    n_prefix = 256
+    span = cfg.n_kv_heads * cfg.head_dim
+    orun = o.OracleRun(om, n_prefix + 8)
+    drun = ForwardRun(dm, context_length=n_prefix + 8)
+    for layer in range(cfg.n_layers):
+        k = synth.normal(7, 1000 + layer, n_prefix * span, 0.0, 50.0)
+        v = synth.normal(7, 2000 + layer, n_prefix * span, 0.0, 50.0)
+        orun.set_prefix(layer, k, v, n_prefix)
+        drun.set_prefix(layer, k, v, n_prefix)
+    toks = synth.tokens(7, 5, 4, cfg.vocab)
+    for t in toks:
+        orun.push_token(int(t))
+        drun.push_token(int(t))
+        within(drun.position_logits(), orun.position_logits())
+    assert len(drun) == n_prefix + 4
+
+
+def test_fail_closed_and_commit_contract(tiny):
+    from faber_runtime_b200 import FaberError, ForwardRun, OracleError
+    _, dm, _ = tiny
+    run = ForwardRun(dm, context_length=4)
+    with pytest.raises(OracleError):
+        run.position_logits()
+    with pytest.raises(OracleError):
+        run.push_tokens([])
+    with pytest.raises(OracleError):
+        run.push_token(32000)
+    with pytest.raises(OracleError):
+        run.push_token(-1)
+    assert len(run) == 0
+    run.push_tokens([1, 2, 3, 4])
+    with pytest.raises(FaberError) as e:
+        run.push_token(5)
+    assert e.value.code == 2 and len(run) == 4
+    # SequenceState::commit
+    assert run.commit(10, 0, 1) == "applied"
+    assert run.commit(10, 0, 1) == "idempotent_replay"
+    with pytest.raises(FaberError):
+        run.commit(11, 3, 2)  # out of order
+    with pytest.raises(FaberError):
+        run.commit(11, 1, 5)  # KV generation gap
+    with pytest.raises(FaberError):
+        run.commit(11, 1, 2, publication_boundary=0)
+    assert run.commit(11, 1, 2) == "applied"
+    run.reset()
+    assert len(run) == 0
+    run.push_token(3)
+    assert len(run) == 1
