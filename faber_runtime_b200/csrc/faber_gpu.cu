@@ -48,7 +48,39 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // GEMV launch
 // ---------------------------------------------------------------------------
 template <int WL, int PRO, int EPI>
+void launch_gemv_pipe(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  auto kern = gemv_pipe_kernel<WL, PRO, EPI>;
+  static thread_local std::map<int, bool> attr_done;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+    attr_done[dev] = true;
+  }
+  const PipeLayout L = pipe_layout(a.nb);
+  require(L.total <= 232448, FABER_STATUS_UNSUPPORTED, "GEMV input too long for shared-memory staging");
+  // two CTAs per SM: 16 consumer warps hide the dequant dependency chains
+  const int per_sm = 2 * L.total <= 227 * 1024 ? 2 : 1;
+  const int grid = std::max(1, std::min(a.n_tiles, per_sm * device_info().sms));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPipeThreads);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  FABER_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+template <int WL, int PRO, int EPI>
 void launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  if constexpr (WL != WL_F16) {
+    launch_gemv_pipe<WL, PRO, EPI>(a, stream, pdl);
+    return;
+  } else {
   auto kern = gemv_kernel<WL, PRO, EPI>;
   // per device: attribute set once; occupancy cached per shared-memory size
   static thread_local std::map<int, std::map<size_t, int>> occ_cache;
@@ -80,6 +112,7 @@ void launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   FABER_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  }
 }
 
 template <class K, class... Args>

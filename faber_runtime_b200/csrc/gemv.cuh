@@ -5,20 +5,23 @@
 // (src/dequant.rs:194-217) after metal_f16_round_weights
 // (src/cpu_oracle.rs:356-360).
 //
-// Data path per warp and 16-row tile:
-//   * 16-byte streaming loads of the Q4_K tile (headers + quants); each lane
-//     owns one 32-byte quant chunk (two sub-blocks) of two rows;
-//   * per weight: a mask-or against the 2^23 magic turns a nibble into an
-//     exact float, then one packed f32x2 FMA computes d1*q - m1 with a single
-//     rounding (d1*q is exact, so this equals the reference's separately
-//     rounded multiply then subtract), and one cvt.rn.f16x2 rounds two
-//     weights to f16 exactly as the reference does — the packed result is
-//     already the tensor-core A operand;
+// Data path (one producer warp + 8 consumer warps per CTA, 2 CTAs per SM):
+//   * the producer streams 2304-byte tile items (16 rows x one super-block:
+//     16 headers, then 16 x 128 quant bytes) with bulk TMA copies into a
+//     3-4 stage shared-memory ring guarded by mbarriers (no multicast);
+//   * each consumer lane owns one 32-byte quant chunk (two sub-blocks) of
+//     two rows; per 32-bit quant word it forms exact weights with
+//       (w & 0x000F000F) | 0x64006400  -> (1024 + q, 1024 + q') as f16x2,
+//       fma.f16x2(1024 + q, sc, -1024 sc) -> sc*q exactly (<= 945),
+//       fma.rn.f32.f16(d, sc*q, -m1)   -> RN32(d1*q - m1), the reference's
+//                                          separately rounded value,
+//       cvt.rn.f16x2.f32               -> the f16-rounded weight pair,
+//     which is already the tensor-core A operand;
 //   * x is staged once per CTA in shared memory as an exact two-term f16
 //     split (x*2^-s = hi + lo, s a power-of-two scale from max|x|), and
 //     mma.sync m16n8k16 (f16 x f16 -> f32) multiplies the 16x16 weight tile
-//     by [hi, lo]: column 0 and 1 of the accumulator sum to y*2^-s. The
-//     tensor core is the reduction engine (no shuffles);
+//     by [hi, lo]: accumulator columns 0 and 1 sum to y*2^-s. The tensor
+//     core is the reduction engine;
 //   * warps split K (super-blocks) and the CTA reduces the 8 partial tiles
 //     in shared memory in a fixed order (deterministic), then runs a fused
 //     epilogue (store / residual add / RoPE + KV-cache append / SwiGLU /
@@ -26,6 +29,14 @@
 #pragma once
 
 #include "common.cuh"
+
+// Weight formation: 3 = f16 magics + exact sc*q + mixed-precision FMA (the
+// default, fewest ALU-pipe instructions); 1 = one mask-or per nibble against
+// the 2^23 f32 magic; 2 = byte permute; 0 = plain C expressions. All four
+// produce bit-identical weights.
+#ifndef FABER_DQ_MODE
+#define FABER_DQ_MODE 3
+#endif
 
 namespace faber {
 
@@ -88,26 +99,41 @@ __host__ __device__ inline int gemv_xs_halves(int nb) {
 // ---------------------------------------------------------------------------
 // Block reductions (fixed order: deterministic and identical in every CTA)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ double block_sum_f64(double v, double* red) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  double s = 0.0;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
-  return s;
+// The 256 threads that stage x and compute: the whole CTA (register kernel)
+// or the 8 consumer warps of the pipelined kernel (named barrier 1, so the
+// producer warp never takes part).
+template <bool NAMED>
+__device__ __forceinline__ void cbar() {
+  if (NAMED) asm volatile("bar.sync 1, 256;" ::: "memory");
+  else __syncthreads();
 }
 
-__device__ __forceinline__ float block_max_f32(float v, float* red) {
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+template <bool NAMED>
+__device__ __forceinline__ void block_sum_max(double& v, float& m, double* redd, float* redf) {
+  for (int o = 16; o > 0; o >>= 1) {
+    v += __shfl_xor_sync(0xffffffffu, v, o);
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float m = 0.0f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
-  return m;
+  cbar<NAMED>();
+  if (lane == 0) {
+    redd[warp] = v;
+    redf[warp] = m;
+  }
+  cbar<NAMED>();
+  double s = 0.0;
+  float mm = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kGemvWarps; ++w) {
+    s += redd[w];
+    mm = fmaxf(mm, redf[w]);
+  }
+  v = s;
+  m = mm;
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
 // Power-of-two scale that brings max|x| into [2^13, 2^14).
@@ -119,65 +145,144 @@ __device__ __forceinline__ int split_shift(float bound) {
   return max(-100, min(100, s));
 }
 
-// Stage x (or rms_norm(x) * w) into shared memory as the hi/lo f16 split.
-// Returns the output scale 2^s.
+// Element i of the GEMV input before normalization (x, or x + x2).
 template <int PRO>
+__device__ __forceinline__ float4 load_x4(const GemvArgs& a, int i4) {
+  float4 v = reinterpret_cast<const float4*>(a.x)[i4];
+  if (PRO == PRO_NORM_RES) {
+    const float4 u = reinterpret_cast<const float4*>(a.x2)[i4];
+    v = make_float4(v.x + u.x, v.y + u.y, v.z + u.z, v.w + u.w);
+  }
+  return v;
+}
+
+template <int PRO>
+__device__ __forceinline__ float load_x1(const GemvArgs& a, int i) {
+  return (PRO == PRO_NORM_RES) ? a.x[i] + a.x2[i] : a.x[i];
+}
+
+// Normalized value: rms_norm's x*scale*w with two rounded products
+// (src/decoder_ops.rs:140-143).
+template <int PRO>
+__device__ __forceinline__ float norm1(float x, float scale, float w) {
+  return PRO == PRO_PLAIN ? x : __fmul_rn(__fmul_rn(x, scale), w);
+}
+
+__device__ __forceinline__ void split_store(float v0, float v1, float v2, float v3, float in_s,
+                                            __half* xh, __half* xl, int idx) {
+  const __half2 h01 = __floats2half2_rn(v0 * in_s, v1 * in_s);
+  const __half2 h23 = __floats2half2_rn(v2 * in_s, v3 * in_s);
+  const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+  const __half2 l01 = __floats2half2_rn(v0 * in_s - f01.x, v1 * in_s - f01.y);
+  const __half2 l23 = __floats2half2_rn(v2 * in_s - f23.x, v3 * in_s - f23.y);
+  uint2 hv, lv;
+  hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+  hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+  lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+  lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+  *reinterpret_cast<uint2*>(xh + idx) = hv;
+  *reinterpret_cast<uint2*>(xl + idx) = lv;
+}
+
+// Stage x (or rms_norm(x) * w) into shared memory as the hi/lo f16 split,
+// 256 threads. Pass 1 reduces sum of squares (f64) and a max bound; pass 2
+// writes the split. Returns the output scale 2^s.
+// PERM stores each group of four elements as (0, 2, 1, 3): the order in which
+// the f16-magic dequant (two nibbles per mask, bytes 0/2 then 1/3) fills the
+// tensor-core A fragments.
+template <int PRO, bool NAMED, bool PERM>
 __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd, float* redf) {
+  constexpr int NT = kGemvThreads;
   const int n = a.n_cols;
+  const int tid = threadIdx.x;
+  const bool vec = (n % 4 == 0) && aligned16(a.x) &&
+                   (PRO == PRO_PLAIN || aligned16(a.norm_w)) &&
+                   (PRO != PRO_NORM_RES || aligned16(a.x2));
   double ss = 0.0;
   float mx = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = (PRO == PRO_NORM_RES) ? a.x[i] + a.x2[i] : a.x[i];
-    if (PRO != PRO_PLAIN) {
-      ss += (double)v * (double)v;
-      mx = fmaxf(mx, fabsf(v * a.norm_w[i]));
-    } else {
-      mx = fmaxf(mx, fabsf(v));
+  if (vec) {
+#pragma unroll 4
+    for (int i4 = tid; i4 < n / 4; i4 += NT) {
+      const float4 v = load_x4<PRO>(a, i4);
+      if (PRO != PRO_PLAIN) {
+        const float4 w = reinterpret_cast<const float4*>(a.norm_w)[i4];
+        ss += (double)v.x * (double)v.x;
+        ss += (double)v.y * (double)v.y;
+        ss += (double)v.z * (double)v.z;
+        ss += (double)v.w * (double)v.w;
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * w.x), fabsf(v.y * w.y)),
+                             fmaxf(fabsf(v.z * w.z), fabsf(v.w * w.w))));
+      } else {
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+    }
+  } else {
+    for (int i = tid; i < n; i += NT) {
+      const float v = load_x1<PRO>(a, i);
+      if (PRO != PRO_PLAIN) {
+        ss += (double)v * (double)v;
+        mx = fmaxf(mx, fabsf(v * a.norm_w[i]));
+      } else {
+        mx = fmaxf(mx, fabsf(v));
+      }
     }
   }
-  float scale = 1.0f;
-  float bound;
+  block_sum_max<NAMED>(ss, mx, redd, redf);
+  float scale = 1.0f, bound = mx;
   if (PRO != PRO_PLAIN) {
     // rms_norm (src/decoder_ops.rs:126-144): f64 sum, mean cast to f32,
     // scale = 1/sqrt(mean + eps).
-    const double tot = block_sum_f64(ss, redd);
-    const float mean = (float)(tot / (double)n);
+    const float mean = (float)(ss / (double)n);
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-    bound = block_max_f32(mx, redf) * scale * 1.001f;
-  } else {
-    bound = block_max_f32(mx, redf);
+    bound = mx * scale * 1.001f;
   }
   const int s = split_shift(bound);
   const float in_s = ldexpf(1.0f, -s);
+  const bool cta0 = blockIdx.x == 0;
+  // zero halo in front of x and the tail after it
   const int total = kXPad + a.nb * 256;
-  for (int p = threadIdx.x; p < total / 2; p += blockDim.x) {
-    const int v0 = 2 * p - kXPad;
-    float val[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int v = v0 + k;
-      float x = 0.0f;
-      if (v >= 0 && v < n) {
-        x = a.x[v];
-        if (PRO == PRO_NORM_RES) {
-          x = x + a.x2[v];
-          if (blockIdx.x == 0) a.x_sum_out[v] = x;
-        }
-        if (PRO != PRO_PLAIN) {
-          x = __fmul_rn(__fmul_rn(x, scale), a.norm_w[v]);
-          if (a.x_norm_out && blockIdx.x == 0) a.x_norm_out[v] = x;
-        }
-      }
-      val[k] = x * in_s;
-    }
-    const __half2 hi = __floats2half2_rn(val[0], val[1]);
-    const float2 hf = __half22float2(hi);
-    const __half2 lo = __floats2half2_rn(val[0] - hf.x, val[1] - hf.y);
-    const int idx = xs_index(2 * p);
-    *reinterpret_cast<__half2*>(xh + idx) = hi;
-    *reinterpret_cast<__half2*>(xl + idx) = lo;
+  for (int p = tid; p < kXPad; p += NT) {
+    xh[xs_index(p)] = __float2half(0.0f);
+    xl[xs_index(p)] = __float2half(0.0f);
   }
-  __syncthreads();
+  for (int p = kXPad + n + tid; p < total; p += NT) {
+    xh[xs_index(p)] = __float2half(0.0f);
+    xl[xs_index(p)] = __float2half(0.0f);
+  }
+  if (vec) {
+#pragma unroll 4
+    for (int i4 = tid; i4 < n / 4; i4 += NT) {
+      const float4 v = load_x4<PRO>(a, i4);
+      float4 y = v;
+      if (PRO != PRO_PLAIN) {
+        const float4 w = reinterpret_cast<const float4*>(a.norm_w)[i4];
+        y = make_float4(norm1<PRO>(v.x, scale, w.x), norm1<PRO>(v.y, scale, w.y),
+                        norm1<PRO>(v.z, scale, w.z), norm1<PRO>(v.w, scale, w.w));
+      }
+      if (cta0) {
+        if (PRO == PRO_NORM_RES) reinterpret_cast<float4*>(a.x_sum_out)[i4] = v;
+        if (PRO != PRO_PLAIN && a.x_norm_out) reinterpret_cast<float4*>(a.x_norm_out)[i4] = y;
+      }
+      if (PERM) split_store(y.x, y.z, y.y, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
+      else split_store(y.x, y.y, y.z, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
+    }
+  } else {
+    for (int i = tid; i < n; i += NT) {
+      const float v = load_x1<PRO>(a, i);
+      const float y = PRO == PRO_PLAIN ? v : norm1<PRO>(v, scale, a.norm_w[i]);
+      if (cta0) {
+        if (PRO == PRO_NORM_RES) a.x_sum_out[i] = v;
+        if (PRO != PRO_PLAIN && a.x_norm_out) a.x_norm_out[i] = y;
+      }
+      const float sv = y * in_s;
+      const __half hi = __float2half_rn(sv);
+      const int r = i & 3;
+      const int pos = PERM ? ((i & ~3) | (r == 1 ? 2 : (r == 2 ? 1 : r))) : i;
+      xh[xs_index(kXPad + pos)] = hi;
+      xl[xs_index(kXPad + pos)] = __float2half_rn(sv - __half2float(hi));
+    }
+  }
+  cbar<NAMED>();
   return ldexpf(1.0f, s);
 }
 
@@ -248,10 +353,15 @@ __device__ __forceinline__ RowScales row_scales(const uint4 h, int t) {
   const float d1 = __fmul_rn(d, sc_lo), d2 = __fmul_rn(d, sc_hi);
   const float m1 = __fmul_rn(dmin, m_lo), m2 = __fmul_rn(dmin, m_hi);
   RowScales r;
+#if FABER_DQ_MODE == 2
+  r.lo01 = r.lo23 = make_float2(d1, d1);
+  r.hi01 = r.hi23 = make_float2(d2, d2);
+#else
   r.lo01 = make_float2(d1, d1 * 0x1p-8f);
   r.lo23 = make_float2(d1 * 0x1p-16f, d1 * 0x1p-12f);
   r.hi01 = make_float2(d2 * 0x1p-4f, d2 * 0x1p-12f);
   r.hi23 = make_float2(d2 * 0x1p-8f, d2 * 0x1p-16f);
+#endif
   r.nm1 = make_float2(-m1, -m1);
   r.nm2 = make_float2(-m2, -m2);
   return r;
@@ -260,15 +370,50 @@ __device__ __forceinline__ RowScales row_scales(const uint4 h, int t) {
 // Dequantize the 8 nibbles of one quant word into four f16x2 A-operand
 // registers: lo = (e, e+1), (e+2, e+3) of the low sub-block; hi = the same
 // slots of the high sub-block.
+// One-instruction (w & MASK) | magic, with the magic in a register operand.
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t magic) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w), "n"(MASK), "r"(magic));
+  return d;
+}
+
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "n"(SEL));
+  return d;
+}
+
 __device__ __forceinline__ void dequant_word(uint32_t w, const RowScales& s, uint32_t& lo0,
-                                             uint32_t& lo2, uint32_t& hi0, uint32_t& hi2) {
-  constexpr uint32_t M = 0x4b000000u;  // 2^23
+                                             uint32_t& lo2, uint32_t& hi0, uint32_t& hi2,
+                                             uint32_t magic) {
   const float2 negM = make_float2(-8388608.0f, -8388608.0f);
+  float2 f01, f23, h01, h23;
+#if FABER_DQ_MODE == 2
+  // byte permute: each nibble (pre-masked to a byte) lands in the magic's
+  // low mantissa byte, so every weight uses the unscaled d1 / d2
+  const uint32_t vl = w & 0x0f0f0f0fu, vh = (w >> 4) & 0x0f0f0f0fu;
+  f01 = make_float2(u2f(prmt<0x7540>(vl, magic)), u2f(prmt<0x7541>(vl, magic)));
+  f23 = make_float2(u2f(prmt<0x7542>(vl, magic)), u2f(prmt<0x7543>(vl, magic)));
+  h01 = make_float2(u2f(prmt<0x7540>(vh, magic)), u2f(prmt<0x7541>(vh, magic)));
+  h23 = make_float2(u2f(prmt<0x7542>(vh, magic)), u2f(prmt<0x7543>(vh, magic)));
+#elif FABER_DQ_MODE == 1
+  // the nibble stays at its bit position (<= bit 19) inside the 2^23 magic's
+  // mantissa; the per-position power of two is folded into the scale
   const uint32_t u = w >> 12;
-  float2 f01 = make_float2(u2f((w & 0x0000000fu) | M), u2f((w & 0x00000f00u) | M));
-  float2 f23 = make_float2(u2f((w & 0x000f0000u) | M), u2f((u & 0x0000f000u) | M));
-  float2 h01 = make_float2(u2f((w & 0x000000f0u) | M), u2f((w & 0x0000f000u) | M));
-  float2 h23 = make_float2(u2f((u & 0x00000f00u) | M), u2f((u & 0x000f0000u) | M));
+  f01 = make_float2(u2f(and_or<0x0000000fu>(w, magic)), u2f(and_or<0x00000f00u>(w, magic)));
+  f23 = make_float2(u2f(and_or<0x000f0000u>(w, magic)), u2f(and_or<0x0000f000u>(u, magic)));
+  h01 = make_float2(u2f(and_or<0x000000f0u>(w, magic)), u2f(and_or<0x0000f000u>(w, magic)));
+  h23 = make_float2(u2f(and_or<0x00000f00u>(u, magic)), u2f(and_or<0x000f0000u>(u, magic)));
+#else
+  const uint32_t M = magic;
+  const uint32_t u = w >> 12;
+  f01 = make_float2(u2f((w & 0x0000000fu) | M), u2f((w & 0x00000f00u) | M));
+  f23 = make_float2(u2f((w & 0x000f0000u) | M), u2f((u & 0x0000f000u) | M));
+  h01 = make_float2(u2f((w & 0x000000f0u) | M), u2f((w & 0x0000f000u) | M));
+  h23 = make_float2(u2f((u & 0x00000f00u) | M), u2f((u & 0x000f0000u) | M));
+#endif
   f01 = __ffma2_rn(__fadd2_rn(f01, negM), s.lo01, s.nm1);
   f23 = __ffma2_rn(__fadd2_rn(f23, negM), s.lo23, s.nm1);
   h01 = __ffma2_rn(__fadd2_rn(h01, negM), s.hi01, s.nm2);
@@ -279,40 +424,197 @@ __device__ __forceinline__ void dequant_word(uint32_t w, const RowScales& s, uin
   hi2 = pack_half2(h23.x, h23.y);
 }
 
+// ---------------------------------------------------------------------------
+// Mode 3: two nibbles per mask via f16 magics, exact sc*q in f16, and a
+// mixed-precision FMA for RN32(d*(sc*q) - m1).
+//   (w & 0x000F000F) | 0x64006400 = (1024 + q, 1024 + q') as f16x2;
+//   (w & 0x00F000F0) | 0x54005400 = (64 + q, 64 + q') (high nibbles);
+//   fma.f16x2((K + q), sc, -K*sc) = sc*q exactly (<= 945 < 2048);
+//   fma.rn.f32.f16(d, sc*q, -m1) = RN32(d*sc*q - m1): d*sc*q is exact in
+//   f32 (22 bits) and equals d1*q of the reference, so one rounding here is
+//   the reference's d1*q - m1 (src/dequant.rs:204-211).
+// A word yields pairs (e, e+2) from bytes 0/2 and (e+1, e+3) from bytes 1/3.
+// ---------------------------------------------------------------------------
+struct LaneConst {
+  uint32_t sel;    // byte permute that gathers this lane's two scale bytes
+  uint32_t m1024;  // 0x64006400
+  uint32_t m64;    // 0x54005400
+};
+
+struct RowScales3 {
+  uint32_t sclo2, clo2, schi2, chi2;  // f16x2 (sc, sc), (-K sc, -K sc) per sub-block
+  float nm1, nm2;                     // -m1, -m2
+  uint32_t dword;                     // header word 0: d (f16) in the low half
+};
+
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t prmt_r(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// RN32(lo16(dword) * q16 + c) for both halves q16 of `q2`.
+__device__ __forceinline__ float2 mixed_fma_pair(uint32_t q2, uint32_t dword, float c) {
+  float x, y;
+  asm("{\n .reg .b16 q0, q1, d0, d1;\n mov.b32 {q0, q1}, %2;\n mov.b32 {d0, d1}, %3;\n"
+      " fma.rn.f32.f16 %0, d0, q0, %4;\n fma.rn.f32.f16 %1, d0, q1, %4;\n}"
+      : "=f"(x), "=f"(y)
+      : "r"(q2), "r"(dword), "f"(c));
+  return make_float2(x, y);
+}
+
+// RN32(hi16(dword) * q16_lo) and RN32(hi16(dword) * q16_hi): dmin * m (exact).
+__device__ __forceinline__ float2 mixed_mul_hi_pair(uint32_t q2, uint32_t dword) {
+  float x, y;
+  asm("{\n .reg .b16 q0, q1, d0, d1;\n mov.b32 {q0, q1}, %2;\n mov.b32 {d0, d1}, %3;\n"
+      " fma.rn.f32.f16 %0, d1, q0, 0f80000000;\n fma.rn.f32.f16 %1, d1, q1, 0f80000000;\n}"
+      : "=f"(x), "=f"(y)
+      : "r"(q2), "r"(dword));
+  return make_float2(x, y);
+}
+
+__device__ __forceinline__ RowScales3 row_scales3(const uint4 h, int t, const LaneConst& lc) {
+  const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
+  uint32_t sc, mm;  // get_scale_min_k4 for this lane's 4-index half, as packed bytes
+  if (t < 2) {
+    sc = s0 & 0x3f3f3f3fu;
+    mm = s1 & 0x3f3f3f3fu;
+  } else {
+    sc = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
+    mm = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
+  }
+  // (1024 + v_lo, 1024 + v_hi) as f16x2, then minus 1024: exact small ints
+  const uint32_t k1024 = 0x64006400u;
+  const uint32_t scp = hsub2_u(prmt_r(sc, lc.m1024, lc.sel), k1024);
+  const uint32_t mp = hsub2_u(prmt_r(mm, lc.m1024, lc.sel), k1024);
+  RowScales3 r;
+  r.sclo2 = prmt<0x1010>(scp, 0);  // (sc_lo, sc_lo)
+  r.schi2 = prmt<0x3232>(scp, 0);  // (sc_hi, sc_hi)
+  r.clo2 = hmul2_u(r.sclo2, 0xe400e400u);  // * -1024
+  r.chi2 = hmul2_u(r.schi2, 0xd400d400u);  // * -64
+  const float2 m12 = mixed_mul_hi_pair(mp, h.x);
+  r.nm1 = -m12.x;
+  r.nm2 = -m12.y;
+  r.dword = h.x;
+  return r;
+}
+
+__device__ __forceinline__ void dequant_word3(uint32_t w, const RowScales3& s, const LaneConst& lc,
+                                              uint32_t& lo0, uint32_t& lo2, uint32_t& hi0,
+                                              uint32_t& hi2) {
+  const uint32_t u = w >> 8;
+  const uint32_t l02 = hfma2_u(and_or<0x000f000fu>(w, lc.m1024), s.sclo2, s.clo2);
+  const uint32_t l13 = hfma2_u(and_or<0x000f000fu>(u, lc.m1024), s.sclo2, s.clo2);
+  const uint32_t h02 = hfma2_u(and_or<0x00f000f0u>(w, lc.m64), s.schi2, s.chi2);
+  const uint32_t h13 = hfma2_u(and_or<0x00f000f0u>(u, lc.m64), s.schi2, s.chi2);
+  const float2 a = mixed_fma_pair(l02, s.dword, s.nm1);
+  const float2 b = mixed_fma_pair(l13, s.dword, s.nm1);
+  const float2 c = mixed_fma_pair(h02, s.dword, s.nm2);
+  const float2 d = mixed_fma_pair(h13, s.dword, s.nm2);
+  lo0 = pack_half2(a.x, a.y);  // (e, e+2)
+  lo2 = pack_half2(b.x, b.y);  // (e+1, e+3)
+  hi0 = pack_half2(c.x, c.y);
+  hi2 = pack_half2(d.x, d.y);
+}
+
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
-// 16 MMAs of one Q4_K item into the warp accumulators.
-__device__ __forceinline__ void q4_compute(const Q4Regs& r, int t, int g, const __half* xsrc,
-                                           int xbase, float acc[4]) {
+// 16 MMAs of one Q4_K item into four independent accumulator chains (MMA m
+// goes to chain m & 3, so consecutive MMAs do not wait on each other).
+// B fragments come from lane groups 0 (hi column) and 1 (lo column); the
+// other groups load the same rows (a free shared-memory broadcast, no
+// predication) and their values only reach accumulator columns 2..7, which
+// are never read.
+__device__ __forceinline__ void q4_compute(const Q4Regs& r, int t, const __half* xsrc, int xbase,
+                                           float (&acc)[4][4], const LaneConst& lc) {
+#if FABER_DQ_MODE == 3
+  const RowScales3 sA = row_scales3(r.hA, t, lc);
+  const RowScales3 sB = row_scales3(r.hB, t, lc);
+#else
+  const uint32_t magic = lc.m1024;
   const RowScales sA = row_scales(r.hA, t);
   const RowScales sB = row_scales(r.hB, t);
+#endif
 #pragma unroll
   for (int pp = 0; pp < 2; ++pp) {
     const uint4 qa = pp ? r.qA1 : r.qA0;
     const uint4 qb = pp ? r.qB1 : r.qB0;
-    // B fragments: elements e = 64t + 32n + 16pp + 4i of this super-block.
-    uint4 xb_lo0 = make_uint4(0, 0, 0, 0), xb_lo1 = xb_lo0, xb_hi0 = xb_lo0, xb_hi1 = xb_lo0;
-    if (g < 2) {
-      const int e0 = xbase + 64 * t + 16 * pp;
-      xb_lo0 = *reinterpret_cast<const uint4*>(xsrc + xs_index(e0));
-      xb_lo1 = *reinterpret_cast<const uint4*>(xsrc + xs_index(e0 + 8));
-      xb_hi0 = *reinterpret_cast<const uint4*>(xsrc + xs_index(e0 + 32));
-      xb_hi1 = *reinterpret_cast<const uint4*>(xsrc + xs_index(e0 + 40));
+    // B fragments: elements e = 64t + 32n + 16pp + 4i of this super-block;
+    // v0 is a multiple of 16, so +8 stays inside its 64-group.
+    uint4 xb_lo0, xb_lo1, xb_hi0, xb_hi1;
+    {
+      const int v0 = xbase + 64 * t + 16 * pp;
+      const int p0 = xs_index(v0), p1 = xs_index(v0 + 32);
+      xb_lo0 = *reinterpret_cast<const uint4*>(xsrc + p0);
+      xb_lo1 = *reinterpret_cast<const uint4*>(xsrc + p0 + 8);
+      xb_hi0 = *reinterpret_cast<const uint4*>(xsrc + p1);
+      xb_hi1 = *reinterpret_cast<const uint4*>(xsrc + p1 + 8);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t aL0, aL2, aH0, aH2, bL0, bL2, bH0, bH2;
-      dequant_word(word_of(qa, i), sA, aL0, aL2, aH0, aH2);
-      dequant_word(word_of(qb, i), sB, bL0, bL2, bH0, bH2);
+#if FABER_DQ_MODE == 3
+      dequant_word3(word_of(qa, i), sA, lc, aL0, aL2, aH0, aH2);
+      dequant_word3(word_of(qb, i), sB, lc, bL0, bL2, bH0, bH2);
+#else
+      dequant_word(word_of(qa, i), sA, aL0, aL2, aH0, aH2, magic);
+      dequant_word(word_of(qb, i), sB, bL0, bL2, bH0, bH2, magic);
+#endif
       const uint4& xl = (i < 2) ? xb_lo0 : xb_lo1;
       const uint4& xh = (i < 2) ? xb_hi0 : xb_hi1;
       const uint32_t xl0 = (i & 1) ? xl.z : xl.x, xl1 = (i & 1) ? xl.w : xl.y;
       const uint32_t xh0 = (i & 1) ? xh.z : xh.x, xh1 = (i & 1) ? xh.w : xh.y;
-      mma_16816(acc[0], acc[1], acc[2], acc[3], aL0, bL0, aL2, bL2, xl0, xl1);
-      mma_16816(acc[0], acc[1], acc[2], acc[3], aH0, bH0, aH2, bH2, xh0, xh1);
+      float* cl = acc[(2 * i) & 3];
+      float* ch = acc[(2 * i + 1) & 3];
+      mma_16816(cl[0], cl[1], cl[2], cl[3], aL0, bL0, aL2, bL2, xl0, xl1);
+      mma_16816(ch[0], ch[1], ch[2], ch[3], aH0, bH0, aH2, bH2, xh0, xh1);
     }
+  }
+}
+
+// Load one item's registers from the shared-memory ring (the byte layout of
+// the global item: tiled = 16 headers then 16 x 128 quant bytes; native = 16
+// consecutive 144-byte blocks).
+template <int WL>
+__device__ __forceinline__ void q4_lds(const uint8_t* item, int g, int t, Q4Regs& r) {
+  if (WL == WL_TILED) {
+    r.hA = *reinterpret_cast<const uint4*>(item + 16 * g);
+    r.hB = *reinterpret_cast<const uint4*>(item + 16 * (g + 8));
+    const uint8_t* qa = item + 256 + 128 * g + 32 * t;
+    const uint8_t* qb = qa + 128 * 8;
+    r.qA0 = *reinterpret_cast<const uint4*>(qa);
+    r.qA1 = *reinterpret_cast<const uint4*>(qa + 16);
+    r.qB0 = *reinterpret_cast<const uint4*>(qb);
+    r.qB1 = *reinterpret_cast<const uint4*>(qb + 16);
+  } else {
+    const uint8_t* ra = item + kQ4kBlockBytes * g;
+    const uint8_t* rb = item + kQ4kBlockBytes * (g + 8);
+    r.hA = *reinterpret_cast<const uint4*>(ra);
+    r.qA0 = *reinterpret_cast<const uint4*>(ra + 16 + 32 * t);
+    r.qA1 = *reinterpret_cast<const uint4*>(ra + 32 + 32 * t);
+    r.hB = *reinterpret_cast<const uint4*>(rb);
+    r.qB0 = *reinterpret_cast<const uint4*>(rb + 16 + 32 * t);
+    r.qB1 = *reinterpret_cast<const uint4*>(rb + 32 + 32 * t);
   }
 }
 
@@ -476,16 +778,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 
   // Weights do not depend on the previous kernel: start the first loads
   // before waiting on the producer of x.
+  static_assert(WL == WL_F16, "the register-path kernel serves the f16 head only");
   int tile = blockIdx.x;
   const bool have0 = tile < a.n_tiles && warp < a.nb;
-  Q4Regs q4c, q4n;
   F16Regs f16c;
-  if (have0) {
-    if (WL == WL_F16) f16_load(a, tile, warp, g, t, f16c);
-    else q4_load<WL>(a, tile, warp, g, t, q4c);
-  }
+  if (have0) f16_load(a, tile, warp, g, t, f16c);
   pdl_wait();
-  const float out_scale = stage_x<PRO>(a, xh, xl, redd, redf);
+  const float out_scale = stage_x<PRO, false, false>(a, xh, xl, redd, redf);
   pdl_launch_dependents();
   const __half* xsrc = (g == 0) ? xh : xl;
 
@@ -494,22 +793,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const int xoff = a.tile_xoff ? a.tile_xoff[tile] : 0;
     for (int b = warp; b < a.nb; b += kGemvWarps) {
-      int nbb = b + kGemvWarps, nt = tile;
-      if (nbb >= a.nb) {
-        nbb = warp;
-        nt = tile + gridDim.x;
-      }
-      const bool has_next = nt < a.n_tiles && nbb < a.nb;
       const int xbase = kXPad + b * 256 - xoff;
-      if (WL == WL_F16) {
-        // 64 registers per item: no double buffering, occupancy hides latency
-        if (b != warp || tile != (int)blockIdx.x) f16_load(a, tile, b, g, t, f16c);
-        f16_compute(f16c, t, g, xsrc, xbase, acc);
-      } else {
-        if (has_next) q4_load<WL>(a, nt, nbb, g, t, q4n);
-        q4_compute(q4c, t, g, xsrc, xbase, acc);
-        q4c = q4n;
-      }
+      // 64 registers per item: no double buffering, occupancy hides latency
+      if (b != warp || tile != (int)blockIdx.x) f16_load(a, tile, b, g, t, f16c);
+      f16_compute(f16c, t, g, xsrc, xbase, acc);
     }
     float* pb = part + (it & 1) * kGemvWarps * kTileRows;
     if (t == 0) {
@@ -534,6 +821,217 @@ inline size_t gemv_smem_bytes(int nb) {
   return (size_t)2 * gemv_xs_halves(nb) * sizeof(__half) +
          (size_t)2 * kGemvWarps * kTileRows * sizeof(float) + kGemvWarps * sizeof(double) +
          kGemvWarps * sizeof(float) + 16;
+}
+
+// ---------------------------------------------------------------------------
+// Pipelined Q4_K kernel: one producer warp streams tile items with bulk TMA
+// copies (cp.async.bulk, no multicast) into a shared-memory ring guarded by
+// mbarriers; 8 consumer warps dequantize from shared memory. One CTA per SM,
+// persistent over tiles, so that under programmatic dependent launch the
+// next kernel's producer can already stream its weights.
+// ---------------------------------------------------------------------------
+constexpr int kConsumerWarps = kGemvWarps;
+constexpr int kPipeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStageBytes = kConsumerWarps * kTileItemBytes;  // 18 KB
+constexpr int kMaxStages = 4;
+constexpr uint32_t kSpinLimit = 1u << 20;
+
+// Set by a kernel whose bounded wait expired (never in a correct run).
+__device__ int g_pipe_error;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(b)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: after kSpinLimit polls the error word is set and the caller
+// proceeds (every barrier stays balanced, so no other warp can block).
+__device__ __forceinline__ void mbar_wait(uint64_t* b, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(b, parity)) return;
+  atomicExch(&g_pipe_error, 1);
+}
+
+// Streaming bulk copy global -> own CTA's shared memory, completing on an
+// mbarrier; weights are read once, so L2 may evict them first.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+struct PipeLayout {
+  int stages;
+  size_t ring, xs, part, redd, redf, bars, total;
+};
+
+__host__ __device__ inline PipeLayout pipe_layout(int nb) {
+  PipeLayout L;
+  L.stages = nb > 24 ? 3 : kMaxStages;
+  L.ring = 0;
+  L.xs = (size_t)L.stages * kStageBytes;
+  L.part = L.xs + (size_t)2 * gemv_xs_halves(nb) * 2;
+  L.redd = L.part + (size_t)2 * kConsumerWarps * kTileRows * 4;
+  L.redf = L.redd + (size_t)kConsumerWarps * 8;
+  L.bars = (L.redf + (size_t)kConsumerWarps * 4 + 7) & ~(size_t)7;
+  L.total = L.bars + (size_t)2 * kMaxStages * 8;
+  return L;
+}
+
+template <int WL, int PRO, int EPI>
+__global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvArgs a) {
+  static_assert(WL == WL_TILED || WL == WL_NATIVE, "Q4_K layouts only");
+  extern __shared__ __align__(128) unsigned char smem[];
+  const PipeLayout L = pipe_layout(a.nb);
+  uint8_t* ring = smem + L.ring;
+  const int xs_halves = gemv_xs_halves(a.nb);
+  __half* xh = reinterpret_cast<__half*>(smem + L.xs);
+  __half* xl = xh + xs_halves;
+  float* part = reinterpret_cast<float*>(smem + L.part);
+  double* redd = reinterpret_cast<double*>(smem + L.redd);
+  float* redf = reinterpret_cast<float*>(smem + L.redf);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + kMaxStages;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = L.stages;
+  const int R = (a.nb + kConsumerWarps - 1) / kConsumerWarps;  // rounds per tile
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // producer: weights never depend on the previous kernel, so no wait here
+    if (lane == 0) {
+      uint64_t policy;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      int q = 0, s = 0;
+      uint32_t ph = 0;  // parity of the slot's previous use
+      for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+        for (int r = 0; r < R; ++r, ++q) {
+          if (q >= S) mbar_wait(&empty[s], ph);
+          const int b0 = r * kConsumerWarps;
+          const int cnt = min(kConsumerWarps, a.nb - b0);
+          uint8_t* dst = ring + (size_t)s * kStageBytes;
+          if (WL == WL_TILED) {
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * kTileItemBytes));
+            for (int w = 0; w < cnt; ++w)
+              bulk_g2s(dst + w * kTileItemBytes,
+                       a.w + ((size_t)tile * a.nb + b0 + w) * kTileItemBytes, kTileItemBytes,
+                       &full[s], policy);
+          } else {
+            const int rows = min(kTileRows, a.n_rows - tile * kTileRows);
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * rows * kQ4kBlockBytes));
+            for (int w = 0; w < cnt; ++w)
+              for (int i = 0; i < rows; ++i)
+                bulk_g2s(dst + w * kTileItemBytes + i * kQ4kBlockBytes,
+                         a.w + ((size_t)(tile * kTileRows + i) * a.nb + b0 + w) * kQ4kBlockBytes,
+                         kQ4kBlockBytes, &full[s], policy);
+          }
+          if (++s == S) {
+            s = 0;
+            if (q >= S) ph ^= 1u;
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // consumers
+  pdl_wait();
+  const float out_scale = stage_x<PRO, true, (FABER_DQ_MODE == 3)>(a, xh, xl, redd, redf);
+  pdl_launch_dependents();
+  const int g = lane >> 2, t = lane & 3;
+  const __half* xsrc = (g == 0) ? xh : xl;
+  LaneConst lc;  // magics kept in registers (one lop3 per mask-or)
+  {
+    const uint32_t k = 2u * (uint32_t)(t & 1);
+    lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
+#if FABER_DQ_MODE == 3
+    asm("mov.b32 %0, 0x64006400;" : "=r"(lc.m1024));
+#else
+    asm("mov.b32 %0, 0x4b000000;" : "=r"(lc.m1024));
+#endif
+    asm("mov.b32 %0, 0x54005400;" : "=r"(lc.m64));
+  }
+  const uint8_t* my_item = ring + warp * kTileItemBytes;
+  int s = 0, it = 0;
+  uint32_t ph = 0;
+  for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++it) {
+    float acc[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+    const int xoff = a.tile_xoff ? a.tile_xoff[tile] : 0;
+    int xbase = kXPad + warp * 256 - xoff;
+    for (int b = warp; b < R * kConsumerWarps; b += kConsumerWarps, xbase += kConsumerWarps * 256) {
+      mbar_wait(&full[s], ph);
+      if (b < a.nb) {
+        Q4Regs reg;
+        q4_lds<WL>(my_item + (size_t)s * kStageBytes, g, t, reg);
+        q4_compute(reg, t, xsrc, xbase, acc, lc);
+      }
+      // release the slot once every lane has consumed its bytes
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    float* pb = part + (it & 1) * kConsumerWarps * kTileRows;
+    if (t == 0) {
+      const float a0 = (acc[0][0] + acc[0][1]) + (acc[1][0] + acc[1][1]) +
+                       (acc[2][0] + acc[2][1]) + (acc[3][0] + acc[3][1]);
+      const float a1 = (acc[0][2] + acc[0][3]) + (acc[1][2] + acc[1][3]) +
+                       (acc[2][2] + acc[2][3]) + (acc[3][2] + acc[3][3]);
+      pb[warp * kTileRows + g] = a0;
+      pb[warp * kTileRows + g + 8] = a1;
+    }
+    cbar<true>();
+    if (threadIdx.x < 8) {
+      const int p = threadIdx.x;
+      float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        y0 += pb[w * kTileRows + 2 * p];
+        y1 += pb[w * kTileRows + 2 * p + 1];
+      }
+      gemv_epilogue<EPI>(a, tile, p, y0 * out_scale, y1 * out_scale);
+    }
+  }
 }
 
 }  // namespace faber

@@ -112,6 +112,7 @@ struct StepState {
 __global__ void embed_kernel(StepState* st, const __half* __restrict__ embd, int d, int vocab,
                              float* __restrict__ h) {
   pdl_wait();
+  pdl_launch_dependents();
   const int64_t tok = st->input_token;
   const bool ok = tok >= 0 && tok < vocab;
   for (int i = threadIdx.x; i < d; i += blockDim.x)
@@ -123,12 +124,12 @@ __global__ void embed_kernel(StepState* st, const __half* __restrict__ embd, int
     st->n = st->n + 1;
     st->argmax_key = 0ull;
   }
-  pdl_launch_dependents();
 }
 
 // After the logits: the argmax becomes the next input token and is recorded.
 __global__ void finalize_kernel(StepState* st, int64_t* gen, int32_t gen_cap) {
   pdl_wait();
+  pdl_launch_dependents();
   const unsigned long long key = st->argmax_key;
   const int64_t tok = key ? (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : 0;
   st->input_token = tok;
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   __shared__ float stat[kAttnMaxRatio][2];
   __shared__ int is_last;
   pdl_wait();
+  pdl_launch_dependents();
   const int kh = blockIdx.x, split = blockIdx.y;
   const int n_kv = a.st->cur_pos + 1;
   const int active = (n_kv + kAttnChunk - 1) / kAttnChunk;

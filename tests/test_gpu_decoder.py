@@ -93,9 +93,28 @@ def test_tiny_layer_trace(tiny):
             a, b = drun.trace(0, "attn_in"), orun.trace(0, "attn_in")
             ulp = np.abs(a.view(np.int32).astype(np.int64) - b.view(np.int32).astype(np.int64))
             assert ulp.max() <= 1
+        # The first token attends to one key, so every op is a GEMV or an
+        # element-wise step: 1e-3 x RMS holds everywhere. Later tokens mix
+        # near-tied softmax scores, where ~1e-7 relative score differences
+        # (summation order) move the context by up to ~1e-3 relative; the
+        # intermediates are then held to 1e-2 and the logits to 1e-3.
+        tol = 1e-3 if i == 0 else 1e-2
         for layer in range(om.cfg.n_layers):
             for which in ("attn_in", "q_rot", "k_rot", "v", "ctx", "h2", "hh", "h_out"):
-                within(drun.trace(layer, which), orun.trace(layer, which))
+                a, b = drun.trace(layer, which), orun.trace(layer, which)
+                if which in ("k_rot", "v") or (which == "ctx" and i == 0):
+                    # cached in f16 (and the first context is one cached V
+                    # row): an input difference far below tolerance can still
+                    # move the rounding by one f16 ulp
+                    ulp16 = np.spacing(np.abs(b).astype(np.float16)).astype(np.float64)
+                    rms = np.sqrt(np.mean(np.asarray(b, np.float64) ** 2))
+                    err = np.abs(np.asarray(a, np.float64) - b)
+                    assert np.all(err <= tol * rms + ulp16), (layer, which, err.max())
+                else:
+                    try:
+                        within(a, b, tol)
+                    except AssertionError as e:
+                        raise AssertionError(f"token {i} layer {layer} {which}: {e}") from None
     within(drun.position_logits(), orun.position_logits())
 
 
