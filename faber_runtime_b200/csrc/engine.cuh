@@ -21,6 +21,8 @@
 #include <string>
 #include <vector>
 
+#include "attention.cuh"
+
 namespace faber {
 
 // f32 -> f16 (RN-even) on the host; finite inputs and overflow to inf.
@@ -189,6 +191,22 @@ struct FaberGpuSession {
 };
 
 namespace faber {
+
+// Decode attention with the smallest compiled group size (query heads per kv
+// head) that holds this model's ratio.
+template <int HD>
+void launch_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pdl) {
+  const int ratio = a.n_heads / a.n_kv_heads;
+  const dim3 block(kAttnThreads);
+  if (ratio <= 1)
+    launch_pdl(attention_decode_kernel<HD, 1>, grid, block, 0, stream, pdl, a);
+  else if (ratio <= 2)
+    launch_pdl(attention_decode_kernel<HD, 2>, grid, block, 0, stream, pdl, a);
+  else if (ratio <= 4)
+    launch_pdl(attention_decode_kernel<HD, 4>, grid, block, 0, stream, pdl, a);
+  else
+    launch_pdl(attention_decode_kernel<HD, 8>, grid, block, 0, stream, pdl, a);
+}
 
 // ---------------------------------------------------------------------------
 // Model construction
@@ -404,7 +422,7 @@ inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV
   S.device = M.device;
   FABER_CUDA(cudaSetDevice(M.device));
   S.max_ctx = (int)kv.context_length;
-  S.max_splits = (S.max_ctx + kAttnChunk - 1) / kAttnChunk;
+  S.max_splits = attention_splits(device_info().sms, M.Hkvl, S.max_ctx);
   const uint64_t hd = c.head_dim, d = c.d_model;
   const uint64_t kvs = (uint64_t)M.Hkvl * hd;
   const uint64_t cache = (uint64_t)c.n_layers * S.max_ctx * kvs * 2;
@@ -511,9 +529,9 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       a.scale = 1.0f / sqrtf((float)hd);
       const dim3 grid(M.Hkvl, S.max_splits);
       if (hd == 128)
-        launch_pdl(attention_decode_kernel<128>, grid, dim3(kAttnThreads), 0, S.stream, pdl, a);
+        launch_attention<128>(a, grid, S.stream, pdl);
       else
-        launch_pdl(attention_decode_kernel<64>, grid, dim3(kAttnThreads), 0, S.stream, pdl, a);
+        launch_attention<64>(a, grid, S.stream, pdl);
       if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 4 * S.tr_w, S.ctx.p, nq * 4, cudaMemcpyDeviceToDevice, S.stream));
     }
     // O projection (+ residual)

@@ -1,5 +1,5 @@
 // ops.cuh — the other decode kernels: bit-exact Q4_K dequant, f16 rounding,
-// embedding gather, split-K GQA decode attention, step bookkeeping.
+// embedding gather, step bookkeeping.
 #pragma once
 
 #include "common.cuh"
@@ -139,162 +139,6 @@ __global__ void finalize_kernel(StepState* st, int64_t* gen, int32_t gen_cap) {
     st->gen_count = c + 1;
   }
   st->argmax_key = 0ull;
-}
-
-// ---------------------------------------------------------------------------
-// Split-K GQA decode attention (attention_gqa, src/cpu_oracle.rs:711-792)
-// ---------------------------------------------------------------------------
-// Grid (kv_heads, max_splits); CTA (kv head kh, split s) scores positions
-// [64 s, 64 s + 64) for the `ratio` query heads sharing kv head kh
-// (h / ratio == kh, the verified grouping), keeps (max, sum, acc[hd]) per
-// query head, and the last CTA of each kv head merges the splits in split
-// order. score = (q.k) * scale; softmax over positions 0..=pos.
-constexpr int kAttnChunk = 64;
-constexpr int kAttnThreads = 128;
-constexpr int kAttnMaxRatio = 8;
-
-struct AttnArgs {
-  const float* q;          // [H][hd] post-RoPE queries
-  const __half* k;         // this layer's cache [ctx][Hkv*hd]
-  const __half* v;
-  float* ctx;              // [H][hd]
-  float* part;             // scratch [H][max_splits][hd + 2]
-  int32_t* counters;       // scratch [Hkv], zero between uses
-  const StepState* st;
-  int32_t n_heads, n_kv_heads, head_dim, max_splits;
-  float scale;
-};
-
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnArgs a) {
-  constexpr int DPL = HD / 32;  // dims per lane
-  __shared__ float sc[kAttnMaxRatio][kAttnChunk];
-  __shared__ float red[kAttnThreads / 32][kAttnMaxRatio][HD];
-  __shared__ float stat[kAttnMaxRatio][2];
-  __shared__ int is_last;
-  pdl_wait();
-  pdl_launch_dependents();
-  const int kh = blockIdx.x, split = blockIdx.y;
-  const int n_kv = a.st->cur_pos + 1;
-  const int active = (n_kv + kAttnChunk - 1) / kAttnChunk;
-  if (split >= active) return;
-  const int ratio = a.n_heads / a.n_kv_heads;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvs = a.n_kv_heads * HD;
-  const int j0 = split * kAttnChunk, j1 = min(n_kv, j0 + kAttnChunk);
-
-  float qv[kAttnMaxRatio][DPL];
-#pragma unroll
-  for (int r = 0; r < kAttnMaxRatio; ++r)
-#pragma unroll
-    for (int d = 0; d < DPL; ++d)
-      qv[r][d] = r < ratio ? a.q[(size_t)(kh * ratio + r) * HD + lane * DPL + d] : 0.0f;
-
-  // scores: one warp per position, lanes own DPL consecutive dims
-  for (int j = j0 + warp; j < j1; j += kAttnThreads / 32) {
-    const __half* kp = a.k + (size_t)j * kvs + kh * HD + lane * DPL;
-    float kf[DPL];
-#pragma unroll
-    for (int d = 0; d < DPL; d += 2) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(kp + d));
-      kf[d] = f.x;
-      kf[d + 1] = f.y;
-    }
-#pragma unroll
-    for (int r = 0; r < kAttnMaxRatio; ++r) {
-      if (r >= ratio) break;
-      float s = 0.0f;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) s = fmaf(qv[r][d], kf[d], s);
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) sc[r][j - j0] = s * a.scale;
-    }
-  }
-  __syncthreads();
-  // per query head: chunk max and exp-sum (one warp per head)
-  for (int r = warp; r < ratio; r += kAttnThreads / 32) {
-    float m = -INFINITY;
-    for (int j = lane; j < j1 - j0; j += 32) m = fmaxf(m, sc[r][j]);
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.0f;
-    for (int j = lane; j < j1 - j0; j += 32) {
-      const float p = expf(sc[r][j] - m);
-      sc[r][j] = p;
-      l += p;
-    }
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) {
-      stat[r][0] = m;
-      stat[r][1] = l;
-    }
-  }
-  __syncthreads();
-  // acc[r][d] = sum_j p_j v_j[d]: warps split positions, lanes own dims
-  float acc[kAttnMaxRatio][DPL];
-#pragma unroll
-  for (int r = 0; r < kAttnMaxRatio; ++r)
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) acc[r][d] = 0.0f;
-  for (int j = j0 + warp; j < j1; j += kAttnThreads / 32) {
-    const __half* vp = a.v + (size_t)j * kvs + kh * HD + lane * DPL;
-    float vf[DPL];
-#pragma unroll
-    for (int d = 0; d < DPL; d += 2) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vp + d));
-      vf[d] = f.x;
-      vf[d + 1] = f.y;
-    }
-#pragma unroll
-    for (int r = 0; r < kAttnMaxRatio; ++r) {
-      if (r >= ratio) break;
-      const float p = sc[r][j - j0];
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) acc[r][d] = fmaf(p, vf[d], acc[r][d]);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < kAttnMaxRatio; ++r) {
-    if (r >= ratio) break;
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) red[warp][r][lane * DPL + d] = acc[r][d];
-  }
-  __syncthreads();
-  const int stride = HD + 2;
-  for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
-    const int r = idx / HD, d = idx % HD;
-    float s = 0.0f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) s += red[w][r][d];
-    float* p = a.part + ((size_t)(kh * ratio + r) * a.max_splits + split) * stride;
-    p[2 + d] = s;
-    if (d == 0) {
-      p[0] = stat[r][0];
-      p[1] = stat[r][1];
-    }
-  }
-  // the last CTA of this kv head merges all splits in split order
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ticket = atomicAdd(&a.counters[kh], 1);
-    is_last = (ticket == active - 1);
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
-    const int r = idx / HD, d = idx % HD;
-    const float* base = a.part + (size_t)(kh * ratio + r) * a.max_splits * stride;
-    float M = -INFINITY;
-    for (int s = 0; s < active; ++s) M = fmaxf(M, __ldcg(base + s * stride));
-    float L = 0.0f, acc_d = 0.0f;
-    for (int s = 0; s < active; ++s) {
-      const float f = expf(__ldcg(base + s * stride) - M);
-      L = fmaf(__ldcg(base + s * stride + 1), f, L);
-      acc_d = fmaf(__ldcg(base + s * stride + 2 + d), f, acc_d);
-    }
-    a.ctx[(size_t)(kh * ratio + r) * HD + d] = acc_d / L;
-  }
-  if (threadIdx.x == 0) a.counters[kh] = 0;
 }
 
 }  // namespace faber

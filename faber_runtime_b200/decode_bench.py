@@ -1,0 +1,57 @@
+"""Decode-step micro-benchmark: greedy tokens over an installed K/V prefix.
+
+    python -m faber_runtime_b200.decode_bench --layers 32 --ctx 2048 --steps 8
+
+Builds the Llama-2-7B-shape model (optionally cut to ``--layers``), installs
+a ``--ctx``-position K/V prefix in every layer directly (the same seeded
+random rows in each layer, instead of decoding ``--ctx`` tokens), pushes one
+token, then runs ``--warmup`` and ``--steps`` greedy tokens as CUDA-graph
+replays. Each token launches 5 kernels per layer plus embed, head GEMV and
+finalize (5 * layers + 3), which is what an ncu launch list of one token
+holds.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=2)
+    args = ap.parse_args()
+
+    import torch
+
+    from . import LLAMA2_7B, DeviceModel, ForwardRun, synth
+    cfg = LLAMA2_7B.with_layers(args.layers)
+    seed = 20261201
+    model = DeviceModel(cfg, synth.model_tensors(cfg, seed))
+    run = ForwardRun(model, context_length=args.ctx + args.warmup + args.steps + 4)
+    span = cfg.n_kv_heads * cfg.head_dim
+    k = synth.normal(seed, 5000, args.ctx * span, 0.0, 1.0)
+    v = synth.normal(seed, 6000, args.ctx * span, 0.0, 1.0)
+    for layer in range(cfg.n_layers):
+        run.set_prefix(layer, k, v, args.ctx)
+    run.push_token(1)
+    run.greedy(args.warmup)
+    torch.cuda.synchronize()
+    toks, finite = run.greedy(args.steps)
+    ms = run.last_greedy_ms()
+    kv_bytes = cfg.n_layers * 2 * span * 2 * (args.ctx + args.warmup + args.steps // 2)
+    w_bytes = cfg.linear_bytes() + cfg.head_bytes()
+    print(json.dumps({"layers": cfg.n_layers, "ctx": args.ctx, "steps": args.steps,
+                      "ms_per_token": ms / args.steps, "tok_s": args.steps / (ms * 1e-3),
+                      "weight_bytes": w_bytes, "kv_bytes": kv_bytes,
+                      "gbs": (w_bytes + kv_bytes) / (ms / args.steps * 1e-3) / 1e9,
+                      "finite": finite}))
+    run.close()
+    model.close()
+
+
+if __name__ == "__main__":
+    main()

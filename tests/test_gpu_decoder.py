@@ -118,20 +118,32 @@ def test_tiny_layer_trace(tiny):
     within(drun.position_logits(), orun.position_logits())
 
 
-def test_random_norm_weights_gqa_model(cuda):
-    """GQA (16 query heads over 4 kv heads, head_dim 128) with random per-layer
-    norm weights, so the f16 rounding of norms is exercised."""
+GQA_CASES = [
+    # (query heads, kv heads, head_dim, prompt length)
+    (16, 4, 128, 12),   # ratio 4, one attention split
+    (16, 2, 64, 150),   # ratio 8 (the 70B grouping), three splits, ragged last chunk
+    (12, 4, 64, 70),    # ratio 3 (no exact kernel group size), two splits
+    (8, 8, 128, 129),   # ratio 1, the step's own row opens a new split
+]
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,n_prompt", GQA_CASES)
+def test_random_norm_weights_gqa_model(cuda, heads, kv_heads, head_dim, n_prompt):
+    """GQA groupings with random per-layer norm weights (so the f16 rounding
+    of norms is exercised), over prompts that span several 64-position
+    attention splits."""
     import oracle as o
     from faber_runtime_b200 import ForwardRun, ModelConfig, synth
-    cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=4, head_dim=128, ffn=2816,
-                      vocab=4096, tied_head=False, rope_theta=500000.0, name="gqa-test")
+    cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=heads, n_kv_heads=kv_heads,
+                      head_dim=head_dim, ffn=2816, vocab=4096, tied_head=False,
+                      rope_theta=500000.0, name="gqa-test")
     om, dm, _ = build_pair(cfg, 77, norms="random")
-    prompt = synth.tokens(77, 1, 12, cfg.vocab)
+    prompt = synth.tokens(77, 1, n_prompt, cfg.vocab)
     ref_tokens, ref_logits, _ = om.greedy(prompt, 12, want_logits=True)
-    run = ForwardRun(dm, prompt, context_length=64)
+    run = ForwardRun(dm, prompt, context_length=n_prompt + 16)
     toks, fin = run.greedy(12)
     assert fin and toks.tolist() == ref_tokens.tolist()
-    run2 = ForwardRun(dm, prompt, context_length=64)
+    run2 = ForwardRun(dm, prompt, context_length=n_prompt + 16)
     for i in range(12):
         within(run2.position_logits(), ref_logits[i])
         run2.push_token(int(ref_tokens[i]))
