@@ -437,3 +437,139 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_kv_layout_by
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode attention
+//
+// For callers that must not allocate device memory: a host whose device
+// memory is fully accounted up front (a fixed per-device byte budget, where
+// an unaccounted cudaMalloc is a failure), or one on a latency-critical path
+// where cudaMalloc / cudaFree may synchronize the whole device. The scratch
+// that the split-K attention needs (the per-split partials, the merge
+// counters and the position word) lives in one file-scope __device__ array
+// instead of session buffers. That array is part of the module image: every
+// GPU that loads this library holds it (about 2 MiB) until the process exits,
+// whether or not the entry point is ever called.
+// ---------------------------------------------------------------------------
+namespace faber {
+
+constexpr int kStaticAttnMaxHeads = 128;     // query heads
+constexpr int kStaticAttnMaxKvHeads = 128;   // kv heads
+constexpr size_t kStaticAttnStateOff = 0;    // StepState (cur_pos)
+constexpr size_t kStaticAttnCountersOff = 256;
+constexpr size_t kStaticAttnPartOff = kStaticAttnCountersOff + kStaticAttnMaxKvHeads * 4;
+constexpr size_t kStaticAttnPartBytes = size_t(2) << 20;
+constexpr size_t kStaticAttnBytes = kStaticAttnPartOff + kStaticAttnPartBytes;
+constexpr int kStaticAttnMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_static_attn_scratch[kStaticAttnBytes];
+
+// Argument check that builds its message only on failure (the shared
+// require() takes a std::string, which would allocate on every call).
+inline void static_check(bool cond, int code, const char* msg) {
+  if (!cond) throw Error(code, msg);
+}
+
+// Opens one call: the merge counters start at zero and the attention kernel
+// reads the last position from the state word.
+__global__ void static_attn_open_kernel(StepState* st, int32_t* counters, int n_kv_heads,
+                                        int cur_pos) {
+  for (int i = threadIdx.x; i < n_kv_heads; i += blockDim.x) counters[i] = 0;
+  if (threadIdx.x == 0) st->cur_pos = cur_pos;
+}
+
+// Device address of the scratch array on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached in a fixed table.
+inline unsigned char* static_attn_scratch(int dev) {
+  static std::mutex mu;
+  static unsigned char* table[kStaticAttnMaxDevices] = {};
+  static_check(dev >= 0 && dev < kStaticAttnMaxDevices, FABER_STATUS_UNSUPPORTED,
+               "device ordinal above 63 has no scratch slot");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!table[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_attn_scratch);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw Error(FABER_STATUS_CUDA_ERROR,
+                  std::string("cudaGetSymbolAddress(attention scratch) failed: ") +
+                      cudaGetErrorString(e));
+    }
+    table[dev] = static_cast<unsigned char*>(p);
+  }
+  return table[dev];
+}
+
+inline void attention_decode_static(const float* q, const void* k_cache, const void* v_cache,
+                                    float* ctx, uint32_t n_heads, uint32_t n_kv_heads,
+                                    uint32_t head_dim, uint64_t n_kv, cudaStream_t stream) {
+  constexpr int kBad = FABER_STATUS_INVALID_ARGUMENT;
+  static_check(q && k_cache && v_cache && ctx, kBad, "null pointer");
+  static_check(head_dim == 64 || head_dim == 128, kBad, "head_dim must be 64 or 128");
+  static_check(n_kv_heads >= 1 && n_heads >= n_kv_heads && n_heads % n_kv_heads == 0, kBad,
+               "n_heads must be a positive multiple of n_kv_heads");
+  static_check(n_heads / n_kv_heads <= (uint32_t)kAttnMaxRatio, kBad,
+               "more than 8 query heads per kv head");
+  static_check(n_heads <= (uint32_t)kStaticAttnMaxHeads &&
+                   n_kv_heads <= (uint32_t)kStaticAttnMaxKvHeads,
+               kBad, "the static attention scratch holds at most 128 query heads and 128 kv heads");
+  static_check(n_kv >= 1 && n_kv <= (uint64_t)INT32_MAX, kBad, "n_kv must be in [1, 2^31 - 1]");
+  int dev = 0, sms = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  FABER_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  unsigned char* base = static_attn_scratch(dev);
+  // the partial block of one split: every query head's (max, sum, context)
+  const size_t per_split = (size_t)n_heads * (head_dim + 2) * sizeof(float);
+  const int cap = (int)(kStaticAttnPartBytes / per_split);  // >= 31 within the limits above
+  const int splits = std::min(attention_splits(sms, (int)n_kv_heads, (int)n_kv), cap);
+  StepState* st = reinterpret_cast<StepState*>(base + kStaticAttnStateOff);
+  int32_t* counters = reinterpret_cast<int32_t*>(base + kStaticAttnCountersOff);
+  static_attn_open_kernel<<<1, 128, 0, stream>>>(st, counters, (int)n_kv_heads, (int)(n_kv - 1));
+  FABER_CUDA(cudaGetLastError());
+  AttnArgs a = {};
+  a.q = q;
+  a.k = static_cast<const __half*>(k_cache);
+  a.v = static_cast<const __half*>(v_cache);
+  a.ctx = ctx;
+  a.part = reinterpret_cast<float*>(base + kStaticAttnPartOff);
+  a.counters = counters;
+  a.st = st;
+  a.n_heads = (int32_t)n_heads;
+  a.n_kv_heads = (int32_t)n_kv_heads;
+  a.head_dim = (int32_t)head_dim;
+  a.max_splits = splits;
+  a.scale = 1.0f / sqrtf((float)head_dim);
+  const dim3 grid(n_kv_heads, splits);
+  if (head_dim == 128)
+    launch_attention<128>(a, grid, stream, false);
+  else
+    launch_attention<64>(a, grid, stream, false);
+}
+
+}  // namespace faber
+
+extern "C" {
+
+// Not wrapped in the shared guard, whose fault-injection lookup builds a
+// std::string key: the success path allocates neither device nor host memory.
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_attention_decode_static(
+    const float* q, const void* k_cache, const void* v_cache, float* ctx, uint32_t n_heads,
+    uint32_t n_kv_heads, uint32_t head_dim, uint64_t n_kv, void* stream) {
+  try {
+    attention_decode_static(q, k_cache, v_cache, ctx, n_heads, n_kv_heads, head_dim, n_kv,
+                            as_stream(stream));
+    return status(FABER_STATUS_OK);
+  } catch (const Error& e) {
+    g_last_error = std::string("faber_gpu_v2_attention_decode_static: ") + e.what();
+    return status(e.code);
+  } catch (const std::exception& e) {
+    g_last_error = std::string("faber_gpu_v2_attention_decode_static: ") + e.what();
+    return status(FABER_STATUS_PANIC);
+  } catch (...) {
+    g_last_error = "faber_gpu_v2_attention_decode_static: unknown exception";
+    return status(FABER_STATUS_PANIC);
+  }
+}
+
+}  // extern "C"

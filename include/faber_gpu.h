@@ -264,6 +264,48 @@ FaberRtStatusV1 faber_synth_tokens(uint64_t seed, uint64_t stream, uint64_t n, u
 /* The 128-byte ncclUniqueId for a TP group (rank 0 creates, then shares). */
 FaberRtStatusV1 faber_gpu_v2_nccl_unique_id(uint8_t out[128]);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free decode attention. This entry point has no counterpart in
+ * the reference.
+ *
+ * It is the split-K decode attention of a session, for one query row, for
+ * callers that must not allocate device memory. That means a host whose
+ * device memory is fully accounted up front (a fixed per-device byte budget
+ * in which an unaccounted cudaMalloc is a failure), or code on a
+ * latency-critical path where cudaMalloc / cudaFree may synchronize the
+ * whole device.
+ *
+ * Inputs and outputs belong to the caller, all in device memory:
+ *   q      f32 [n_heads][head_dim]  post-RoPE queries;
+ *   k, v   f16 [n_kv][n_kv_heads * head_dim]  the cached keys and values;
+ *   ctx    f32 [n_heads][head_dim]  the attention output.
+ * Query head h uses kv head h / (n_heads / n_kv_heads). The result agrees
+ * with the session path within floating-point summation order.
+ *
+ * Scratch: one static device array of about 2 MiB (split partials, merge
+ * counters, a position word). It is part of the library image, so every GPU
+ * that loads the library holds it until the process exits. Each call clears
+ * the counters first; the other contents are written before they are read.
+ *
+ * Limits: head_dim 64 or 128; n_heads and n_kv_heads at most 128; at most
+ * 8 query heads per kv head; 1 <= n_kv < 2^31. Sizes beyond these return
+ * INVALID_ARGUMENT with a message, before any work is queued.
+ *
+ * Set-up: the first call on a device looks up the array's device address
+ * with that device current. Make that first call before any stream capture
+ * on the device.
+ *
+ * Concurrency: all calls on a device share the array, so calls that overlap
+ * on the GPU (different streams, or different host threads without ordering)
+ * race and give wrong results. Serialize them, for example on one stream.
+ * The call only enqueues work on `stream`; the output is ready when that
+ * stream has reached the call. */
+FaberRtStatusV1 faber_gpu_v2_attention_decode_static(const float* q, const void* k_cache,
+                                                     const void* v_cache, float* ctx,
+                                                     uint32_t n_heads, uint32_t n_kv_heads,
+                                                     uint32_t head_dim, uint64_t n_kv,
+                                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif
