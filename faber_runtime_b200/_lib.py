@@ -76,6 +76,7 @@ SIGNATURES = {
                                               ctypes.POINTER(U64)]),
     "faber_gpu_v2_model_create": (Status, [ctypes.POINTER(ModelConfigC), PP]),
     "faber_gpu_v2_model_set_tensor": (Status, [P, ctypes.c_char_p, U32, P, U64, U64, U64]),
+    "faber_gpu_v2_tp_shard": (Status, [ctypes.POINTER(ModelConfigC), ctypes.c_char_p, P]),
     "faber_gpu_v2_model_finalize": (Status, [P]),
     "faber_gpu_v2_model_free": (Status, [P]),
     "faber_gpu_v2_model_device_bytes": (Status, [P, ctypes.POINTER(U64)]),

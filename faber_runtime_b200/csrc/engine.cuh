@@ -230,6 +230,94 @@ inline void validate_config(const FaberModelConfigV1& c) {
   }
 }
 
+// Tensor-parallel plan of one rank: Q/K/V split by head, gate/up by FFN
+// super-block and the head by vocab rows (column-parallel); O and down by the
+// matching input columns (row-parallel, summed by an all-reduce). Embedding
+// and norms are replicated. Host-only: the same plan serves model upload and
+// the CPU tests of the sharding.
+struct TpPlan {
+  int Hl = 0, Hkvl = 0, Fl = 0, Vl = 0, v0 = 0, f_blk0 = 0, f_blk1 = 0;
+};
+
+inline TpPlan tp_plan(const FaberModelConfigV1& c) {
+  TpPlan P;
+  const int tp = (int)c.tp_size, rank = (int)c.tp_rank;
+  P.Hl = (int)(c.n_heads / c.tp_size);
+  P.Hkvl = (int)(c.n_kv_heads / c.tp_size);
+  if (tp == 1) {
+    P.Fl = (int)c.ffn;
+    P.f_blk0 = 0;
+    P.f_blk1 = (int)((c.ffn + 255) / 256);
+  } else {
+    const int nF = (int)(c.ffn / 256);
+    P.f_blk0 = rank * nF / tp;
+    P.f_blk1 = (rank + 1) * nF / tp;
+    P.Fl = (P.f_blk1 - P.f_blk0) * 256;
+  }
+  P.v0 = (int)((uint64_t)rank * c.vocab / tp);
+  P.Vl = (int)((uint64_t)(rank + 1) * c.vocab / tp) - P.v0;
+  return P;
+}
+
+// Full shape of a named tensor and this rank's block [r0, r0+nr) x [c0, c0+nc).
+struct ShardRange {
+  uint64_t rows = 0, cols = 0, r0 = 0, nr = 0, c0 = 0, nc = 0;
+  bool q4k = false;  // a Q4_K linear (else an f32 vector or the embedding)
+};
+
+inline ShardRange tensor_shard(const FaberModelConfigV1& c, const TpPlan& P,
+                               const std::string& name) {
+  const uint64_t d = c.d_model, hd = c.head_dim, H = c.n_heads, Hkv = c.n_kv_heads, F = c.ffn;
+  const uint64_t rank = c.tp_rank;
+  auto full = [](uint64_t r, uint64_t k, bool q) {
+    ShardRange s;
+    s.rows = r;
+    s.cols = k;
+    s.nr = r;
+    s.nc = k;
+    s.q4k = q;
+    return s;
+  };
+  auto block = [](uint64_t r, uint64_t k, uint64_t r0, uint64_t nr, uint64_t c0, uint64_t nc) {
+    ShardRange s;
+    s.rows = r;
+    s.cols = k;
+    s.r0 = r0;
+    s.nr = nr;
+    s.c0 = c0;
+    s.nc = nc;
+    s.q4k = true;
+    return s;
+  };
+  if (name == "token_embd.weight") return full(c.vocab, d, false);
+  if (name == "output_norm.weight") return full(d, 1, false);
+  if (name == "output.weight") {
+    FABER_ARG(!c.tied_head, "output.weight given for a tied-head model");
+    return block(c.vocab, d, (uint64_t)P.v0, (uint64_t)P.Vl, 0, d);
+  }
+  unsigned layer = 0;
+  char slot[64] = {0};
+  FABER_ARG(std::sscanf(name.c_str(), "blk.%u.%63[a-z_].weight", &layer, slot) == 2 &&
+                layer < c.n_layers,
+            "unknown tensor name " + name);
+  int ls = -1;
+  for (int k = 0; k < LS_N; ++k)
+    if (std::string(slot) == kLayerSlotNames[k]) ls = k;
+  FABER_ARG(ls >= 0, "unknown tensor name " + name);
+  const uint64_t fr0 = (uint64_t)P.f_blk0 * 256, fnr = (uint64_t)(P.f_blk1 - P.f_blk0) * 256;
+  switch (ls) {
+    case LS_ATTN_NORM:
+    case LS_FFN_NORM: return full(d, 1, false);
+    case LS_Q: return block(H * hd, d, rank * P.Hl * hd, P.Hl * hd, 0, d);
+    case LS_K:
+    case LS_V: return block(Hkv * hd, d, rank * P.Hkvl * hd, P.Hkvl * hd, 0, d);
+    case LS_O: return block(d, H * hd, 0, d, rank * P.Hl * hd, P.Hl * hd);
+    case LS_GATE:
+    case LS_UP: return c.tp_size == 1 ? block(F, d, 0, F, 0, d) : block(F, d, fr0, fnr, 0, d);
+    default: return c.tp_size == 1 ? block(d, F, 0, d, 0, F) : block(d, F, 0, d, fr0, fnr);
+  }
+}
+
 // Native block sub-tensor [r0, r0+nr) x [c0, c0+nc) of a [rows][cols] Q4_K
 // tensor (c0, nc multiples of 256, cols % 256 == 0).
 inline std::vector<uint8_t> q4k_shard(const uint8_t* src, uint64_t cols, uint64_t r0, uint64_t nr,
@@ -247,7 +335,6 @@ inline void model_set_tensor(ModelState& M, const std::string& name, uint32_t ty
   const FaberModelConfigV1& c = M.cfg;
   FABER_ARG(!M.finalized, "model already finalized");
   FABER_ARG(data != nullptr || nbytes == 0, "null tensor data");
-  const uint64_t d = c.d_model, hd = c.head_dim;
   auto expect_shape = [&](uint64_t er, uint64_t ec) {
     FABER_ARG(rows == er && cols == ec, name + ": shape [" + std::to_string(rows) + "x" +
                                             std::to_string(cols) + "], expected [" +
@@ -268,66 +355,49 @@ inline void model_set_tensor(ModelState& M, const std::string& name, uint32_t ty
     h.set = true;
   };
   const uint8_t* src = static_cast<const uint8_t*>(data);
-  // Q4_K linear; shard rows [r0, r0+nr) and cols [c0, c0+nc) for this rank.
-  auto q4k = [&](HostTensor& h, uint64_t er, uint64_t ec, uint64_t r0, uint64_t nr, uint64_t c0,
-                 uint64_t nc) {
-    require(type == FABER_GGML_Q4_K, FABER_STATUS_UNSUPPORTED,
-            name + ": only Q4_K linears are supported on this path");
-    expect_shape(er, ec);
-    FABER_ARG((er * ec) % 256 == 0, name + ": element count not a multiple of 256");
-    expect_bytes(er * ec / 256 * kQ4kBlockBytes);
-    h.type = type;
-    if (M.tp == 1) {
-      h.bytes.assign(src, src + nbytes);
-      h.rows = er;
-      h.cols = ec;
-    } else {
-      h.bytes = q4k_shard(src, ec, r0, nr, c0, nc);
-      h.rows = nr;
-      h.cols = nc;
-    }
-    h.set = true;
-  };
+  const TpPlan P = tp_plan(c);
+  const ShardRange sr = tensor_shard(c, P, name);
   if (name == "token_embd.weight") {
     require(type == FABER_GGML_F32, FABER_STATUS_UNSUPPORTED, name + ": expected F32");
-    expect_shape(c.vocab, d);
-    expect_bytes((uint64_t)c.vocab * d * 4);
+    expect_shape(sr.rows, sr.cols);
+    expect_bytes(sr.rows * sr.cols * 4);
     M.st_embd.type = type;
-    M.st_embd.rows = c.vocab;
-    M.st_embd.cols = d;
+    M.st_embd.rows = sr.rows;
+    M.st_embd.cols = sr.cols;
     M.st_embd.bytes.assign(src, src + nbytes);
     M.st_embd.set = true;
     return;
   }
-  if (name == "output_norm.weight") return f32_vec(M.st_out_norm, d);
-  if (name == "output.weight") {
-    FABER_ARG(!c.tied_head, "output.weight given for a tied-head model");
-    return q4k(M.st_output, c.vocab, d, M.v0, M.Vl, 0, d);
+  HostTensor* h = nullptr;
+  if (name == "output_norm.weight") {
+    h = &M.st_out_norm;
+  } else if (name == "output.weight") {
+    h = &M.st_output;
+  } else {
+    unsigned layer = 0;
+    char slot[64] = {0};
+    std::sscanf(name.c_str(), "blk.%u.%63[a-z_].weight", &layer, slot);  // checked by tensor_shard
+    for (int k = 0; k < LS_N; ++k)
+      if (std::string(slot) == kLayerSlotNames[k]) h = &M.staged[layer][(size_t)k];
   }
-  // blk.N.slot.weight
-  unsigned layer = 0;
-  char slot[64] = {0};
-  FABER_ARG(std::sscanf(name.c_str(), "blk.%u.%63[a-z_].weight", &layer, slot) == 2 &&
-                layer < c.n_layers,
-            "unknown tensor name " + name);
-  int ls = -1;
-  for (int k = 0; k < LS_N; ++k)
-    if (std::string(slot) == kLayerSlotNames[k]) ls = k;
-  FABER_ARG(ls >= 0, "unknown tensor name " + name);
-  HostTensor& h = M.staged[layer][(size_t)ls];
-  const uint64_t H = c.n_heads, Hkv = c.n_kv_heads, F = c.ffn;
-  const uint64_t fr0 = (uint64_t)M.f_blk0 * 256, fnr = (uint64_t)(M.f_blk1 - M.f_blk0) * 256;
-  switch (ls) {
-    case LS_ATTN_NORM:
-    case LS_FFN_NORM: return f32_vec(h, d);
-    case LS_Q: return q4k(h, H * hd, d, M.rank * M.Hl * hd, M.Hl * hd, 0, d);
-    case LS_K:
-    case LS_V: return q4k(h, Hkv * hd, d, M.rank * M.Hkvl * hd, M.Hkvl * hd, 0, d);
-    case LS_O: return q4k(h, d, H * hd, 0, d, M.rank * M.Hl * hd, M.Hl * hd);
-    case LS_GATE:
-    case LS_UP: return q4k(h, F, d, fr0, fnr, 0, d);
-    case LS_DOWN: return q4k(h, d, F, 0, d, fr0, fnr);
+  if (!sr.q4k) return f32_vec(*h, sr.rows);
+  // Q4_K linear: this rank's block rows [r0, r0+nr) x cols [c0, c0+nc)
+  require(type == FABER_GGML_Q4_K, FABER_STATUS_UNSUPPORTED,
+          name + ": only Q4_K linears are supported on this path");
+  expect_shape(sr.rows, sr.cols);
+  FABER_ARG((sr.rows * sr.cols) % 256 == 0, name + ": element count not a multiple of 256");
+  expect_bytes(sr.rows * sr.cols / 256 * kQ4kBlockBytes);
+  h->type = type;
+  if (M.tp == 1) {
+    h->bytes.assign(src, src + nbytes);
+    h->rows = sr.rows;
+    h->cols = sr.cols;
+  } else {
+    h->bytes = q4k_shard(src, sr.cols, sr.r0, sr.nr, sr.c0, sr.nc);
+    h->rows = sr.nr;
+    h->cols = sr.nc;
   }
+  h->set = true;
 }
 
 inline uint64_t nblk(const HostTensor& h) { return h.rows * h.cols / 256; }
@@ -821,20 +891,14 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1*
     M.tp = (int)cfg->tp_size;
     M.rank = (int)cfg->tp_rank;
     FABER_CUDA(cudaGetDevice(&M.device));
-    M.Hl = (int)(cfg->n_heads / cfg->tp_size);
-    M.Hkvl = (int)(cfg->n_kv_heads / cfg->tp_size);
-    if (M.tp == 1) {
-      M.Fl = (int)cfg->ffn;
-      M.f_blk0 = 0;
-      M.f_blk1 = (int)((cfg->ffn + 255) / 256);
-    } else {
-      const int nF = (int)(cfg->ffn / 256);
-      M.f_blk0 = M.rank * nF / M.tp;
-      M.f_blk1 = (M.rank + 1) * nF / M.tp;
-      M.Fl = (M.f_blk1 - M.f_blk0) * 256;
-    }
-    M.v0 = (int)((uint64_t)M.rank * cfg->vocab / M.tp);
-    M.Vl = (int)((uint64_t)(M.rank + 1) * cfg->vocab / M.tp) - M.v0;
+    const TpPlan P = tp_plan(*cfg);
+    M.Hl = P.Hl;
+    M.Hkvl = P.Hkvl;
+    M.Fl = P.Fl;
+    M.f_blk0 = P.f_blk0;
+    M.f_blk1 = P.f_blk1;
+    M.v0 = P.v0;
+    M.Vl = P.Vl;
     M.staged.resize(cfg->n_layers);
     if (M.tp > 1) {
       ncclUniqueId id;
@@ -843,6 +907,22 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1*
       FABER_NCCL(ncclCommInitRank(&M.comm, M.tp, id, M.rank));
     }
     *out = m.release();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_tp_shard(const FaberModelConfigV1* cfg, const char* name,
+                                                   uint64_t out[6]) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_tp_shard", [&] {
+    FABER_ARG(cfg && name && out, "null pointer");
+    validate_config(*cfg);
+    const ShardRange sr = tensor_shard(*cfg, tp_plan(*cfg), name);
+    out[0] = sr.rows;
+    out[1] = sr.cols;
+    out[2] = sr.r0;
+    out[3] = sr.nr;
+    out[4] = sr.c0;
+    out[5] = sr.nc;
   });
 }
 

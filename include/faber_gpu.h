@@ -191,6 +191,16 @@ FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1* cfg, FaberGp
 FaberRtStatusV1 faber_gpu_v2_model_set_tensor(FaberGpuModel* m, const char* name,
                                               uint32_t ggml_type, const void* host_data,
                                               uint64_t nbytes, uint64_t rows, uint64_t cols);
+/* This rank's block of a named tensor under tensor parallelism (host only,
+ * no device call): out = {rows, cols, r0, nr, c0, nc}, the full shape and the
+ * rows [r0, r0+nr) x cols [c0, c0+nc) that rank cfg->tp_rank keeps. Q/K/V
+ * split by head, gate/up by FFN super-block and output by vocab row
+ * (column-parallel); attn_output and ffn_down by the matching input columns
+ * (row-parallel, summed across ranks). Vectors and the embedding are whole.
+ * The reference partitions devices (src/partition.rs:115-417) but has no
+ * tensor-parallel plan; this is the plan model_set_tensor applies. */
+FaberRtStatusV1 faber_gpu_v2_tp_shard(const FaberModelConfigV1* cfg, const char* name,
+                                      uint64_t out[6]);
 /* Check coverage (every tensor present, src/cpu_oracle.rs:409-445) and
  * build the per-model device state. */
 FaberRtStatusV1 faber_gpu_v2_model_finalize(FaberGpuModel* m);
