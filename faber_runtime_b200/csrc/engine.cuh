@@ -138,6 +138,11 @@ struct SessionState {
   DevBuf rope;            // [ctx][hd/2] float2
   DevBuf h, h2, q, ctx, hh, logits, logits_full, opart, dpart;
   DevBuf attn_part, attn_counters;
+  // Tensor-parallel exchange: [2][tp][d] epoch-tagged partials (O, down), 8
+  // bytes each, then the consumers' grid-barrier words. Every rank maps every
+  // other rank's buffer (CUDA IPC) and stores its partials there.
+  DevBuf tp_buf;
+  std::vector<unsigned char*> tp_base;  // rank r's buffer in this process
   DevBuf state;           // StepState
   DevBuf gen;             // int64 [max_ctx]
   DevBuf prompt;          // int64 staging for pushes
@@ -169,11 +174,25 @@ struct SessionState {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     destroy_graphs();
+    close_tp_exchange();
     if (pinned) cudaFreeHost(pinned);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (stream) cudaStreamDestroy(stream);
     if (cur >= 0) cudaSetDevice(cur);
+  }
+  // Peers may still be storing into this rank's buffer until every rank has
+  // stopped stepping: a group barrier comes before the mappings go.
+  void close_tp_exchange() {
+    if (tp_base.empty()) return;
+    ncclComm_t comm = m ? m->s.comm : nullptr;
+    if (comm && stream) {
+      ncclAllReduce(tp_buf.p, tp_buf.p, 1, ncclUint8, ncclMax, comm, stream);  // barrier
+      cudaStreamSynchronize(stream);
+    }
+    for (size_t r = 0; r < tp_base.size(); ++r)
+      if (tp_base[r] && tp_base[r] != tp_buf.p) cudaIpcCloseMemHandle(tp_base[r]);
+    tp_base.clear();
   }
   void destroy_graphs() {
     if (g_push) cudaGraphExecDestroy(g_push);
@@ -477,6 +496,61 @@ inline void model_finalize(ModelState& M) {
 // ---------------------------------------------------------------------------
 // Session
 // ---------------------------------------------------------------------------
+// Allocate this rank's exchange buffer, zero it, and map every rank's buffer
+// here: the IPC handles travel in one NCCL all-gather, which also orders
+// every rank's zeroing before any peer can store into its buffer.
+inline void open_tp_exchange(SessionState& S) {
+  ModelState& M = S.m->s;
+  const size_t tp = (size_t)M.tp, d = M.cfg.d_model;
+  // partials, then the grid-barrier words of the consuming kernels
+  S.tp_buf.alloc(2 * tp * d * sizeof(unsigned long long) + 256);
+  FABER_CUDA(cudaMemset(S.tp_buf.p, 0, S.tp_buf.n));  // epoch 0 never matches
+  cudaIpcMemHandle_t mine;
+  FABER_CUDA(cudaIpcGetMemHandle(&mine, S.tp_buf.p));
+  DevBuf hb(sizeof(cudaIpcMemHandle_t) * tp);
+  unsigned char* slot = hb.as<unsigned char>() + sizeof(mine) * (size_t)M.rank;
+  FABER_CUDA(cudaMemcpy(slot, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+  FABER_NCCL(ncclAllGather(slot, hb.p, sizeof(mine), ncclUint8, M.comm, S.stream));
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  std::vector<cudaIpcMemHandle_t> all(tp);
+  FABER_CUDA(cudaMemcpy(all.data(), hb.p, sizeof(mine) * tp, cudaMemcpyDeviceToHost));
+  S.tp_base.assign(tp, nullptr);
+  for (size_t r = 0; r < tp; ++r) {
+    if ((int)r == M.rank) {
+      S.tp_base[r] = S.tp_buf.as<unsigned char>();
+      continue;
+    }
+    void* p = nullptr;
+    FABER_CUDA(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess));
+    S.tp_base[r] = static_cast<unsigned char*>(p);
+  }
+}
+
+// Producer side of exchange `which` (0: O, 1: down) of `layer`.
+inline void tp_publish_args(SessionState& S, GemvArgs& a, int which, uint32_t layer) {
+  ModelState& M = S.m->s;
+  const size_t tp = (size_t)M.tp, d = M.cfg.d_model;
+  a.tp = M.tp;
+  a.tp_stage = (int)(2 * layer) + which;
+  a.tp_stages = (int)(2 * M.cfg.n_layers);
+  a.epoch_ptr = &S.state.as<StepState>()->tp_epoch;
+  for (size_t r = 0; r < tp; ++r)
+    a.peer_dst[r] = reinterpret_cast<unsigned long long*>(S.tp_base[r]) +
+                    ((size_t)which * tp + (size_t)M.rank) * d;
+}
+
+// Consumer side: the next GEMV sums exchange `which` of `layer` into its input.
+inline void tp_consume_args(SessionState& S, GemvArgs& a, int which, uint32_t layer) {
+  ModelState& M = S.m->s;
+  const size_t tp = (size_t)M.tp, d = M.cfg.d_model;
+  a.tp = M.tp;
+  a.tp_stage = (int)(2 * layer) + which;
+  a.tp_stages = (int)(2 * M.cfg.n_layers);
+  a.epoch_ptr = &S.state.as<StepState>()->tp_epoch;
+  a.red = S.tp_buf.as<unsigned long long>() + (size_t)which * tp * d;
+  a.grid_bar = reinterpret_cast<unsigned int*>(S.tp_buf.as<unsigned long long>() + 2 * tp * d);
+}
+
 inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV1& kv) {
   ModelState& M = m->s;
   const FaberModelConfigV1& c = M.cfg;
@@ -536,6 +610,7 @@ inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV
   FABER_CUDA(cudaMallocHost(&S.pinned, 4096 * sizeof(int64_t)));
   S.pinned_n = 4096;
   S.prefix_layers.assign(c.n_layers, 0);
+  if (M.tp > 1) open_tp_exchange(S);
 }
 
 inline StepState* st_ptr(SessionState& S) { return S.state.as<StepState>(); }
@@ -572,10 +647,11 @@ inline void enqueue_push(SessionState& S, bool pdl) {
         a.v_trace = tr + 3 * S.tr_w;
       }
       if (M.tp > 1 && l > 0) {
+        // h = h2 + (previous layer's down partials of every rank)
         a.x = S.h2.as<float>();
-        a.x2 = S.dpart.as<float>();
         a.x_sum_out = S.h.as<float>();
-        launch_gemv<WL_TILED, PRO_NORM_RES, EPI_QKV>(a, S.stream, pdl);
+        tp_consume_args(S, a, 1, l - 1);
+        launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_QKV>(a, S.stream, pdl);
       } else {
         a.x = S.h.as<float>();
         launch_gemv<WL_TILED, PRO_NORM, EPI_QKV>(a, S.stream, pdl);
@@ -609,9 +685,8 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       GemvArgs a = L.o.args();
       a.x = S.ctx.as<float>();
       if (M.tp > 1) {
-        a.out = S.opart.as<float>();
-        launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, S.stream, pdl);
-        FABER_NCCL(ncclAllReduce(S.opart.p, S.opart.p, d, ncclFloat32, ncclSum, M.comm, S.stream));
+        tp_publish_args(S, a, 0, l);
+        launch_gemv<WL_TILED, PRO_PLAIN, EPI_PEERS>(a, S.stream, pdl);
       } else {
         a.out = S.h2.as<float>();
         a.res = S.h.as<float>();
@@ -625,10 +700,11 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       a.eps = c.rms_eps;
       a.out = S.hh.as<float>();
       if (M.tp > 1) {
+        // h2 = h + (this layer's O partials of every rank)
         a.x = S.h.as<float>();
-        a.x2 = S.opart.as<float>();
         a.x_sum_out = S.h2.as<float>();
-        launch_gemv<WL_TILED, PRO_NORM_RES, EPI_SWIGLU>(a, S.stream, pdl && !M.comm);
+        tp_consume_args(S, a, 0, l);
+        launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_SWIGLU>(a, S.stream, pdl);
       } else {
         a.x = S.h2.as<float>();
         launch_gemv<WL_TILED, PRO_NORM, EPI_SWIGLU>(a, S.stream, pdl);
@@ -643,9 +719,8 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       GemvArgs a = L.down.args();
       a.x = S.hh.as<float>();
       if (M.tp > 1) {
-        a.out = S.dpart.as<float>();
-        launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, S.stream, pdl);
-        FABER_NCCL(ncclAllReduce(S.dpart.p, S.dpart.p, d, ncclFloat32, ncclSum, M.comm, S.stream));
+        tp_publish_args(S, a, 1, l);
+        launch_gemv<WL_TILED, PRO_PLAIN, EPI_PEERS>(a, S.stream, pdl);
       } else {
         a.out = S.h.as<float>();
         a.res = S.h2.as<float>();
@@ -681,17 +756,18 @@ inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>
   for (size_t i = 0; i < eog.size(); ++i) a.eog[i] = eog[i];
   const bool res = M.tp > 1;
   if (res) {
+    // h = h2 + (the last layer's down partials of every rank)
     a.x = S.h2.as<float>();
-    a.x2 = S.dpart.as<float>();
     a.x_sum_out = S.h.as<float>();
+    tp_consume_args(S, a, 1, c.n_layers - 1);
   } else {
     a.x = S.h.as<float>();
   }
   if (c.tied_head) {
-    if (res) launch_gemv<WL_F16, PRO_NORM_RES, EPI_LOGITS>(a, S.stream, pdl);
+    if (res) launch_gemv<WL_F16, PRO_NORM_PEERS, EPI_LOGITS>(a, S.stream, pdl);
     else launch_gemv<WL_F16, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
   } else {
-    if (res) launch_gemv<WL_TILED, PRO_NORM_RES, EPI_LOGITS>(a, S.stream, pdl);
+    if (res) launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_LOGITS>(a, S.stream, pdl);
     else launch_gemv<WL_TILED, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
   }
   if (M.tp > 1) {
@@ -700,6 +776,20 @@ inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>
   }
   launch_pdl(finalize_kernel, dim3(1), dim3(1), 0, S.stream, pdl && M.tp == 1, st, S.gen.as<int64_t>(),
              (int32_t)S.max_ctx);
+}
+
+// A device-side bounded wait that expired (pipeline stage or tensor-parallel
+// peer) is reported once the step has run; the flag is cleared.
+inline void check_device_waits() {
+  int err = 0;
+  FABER_CUDA(cudaMemcpyFromSymbol(&err, g_pipe_error, sizeof(int)));
+  if (!err) return;
+  const int zero = 0;
+  FABER_CUDA(cudaMemcpyToSymbol(g_pipe_error, &zero, sizeof(int)));
+  throw Error(FABER_STATUS_TIMEOUT,
+              err == 2   ? "a tensor-parallel peer did not publish its partials in time"
+              : err == 3 ? "a grid barrier wait expired"
+                         : "a device pipeline wait expired");
 }
 
 inline cudaGraphExec_t capture(SessionState& S, const std::function<void()>& body) {
@@ -767,6 +857,7 @@ inline void run_push(SessionState& S, const int64_t* tokens, uint64_t count) {
     }
   }
   FABER_CUDA(cudaStreamSynchronize(S.stream));
+  check_device_waits();
   StepState st;
   FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
   require(st.status == 0, FABER_STATUS_KERNEL_ERROR, "device-side token check failed");
@@ -784,6 +875,7 @@ inline void gather_logits(SessionState& S, float* host, uint64_t cap) {
     FABER_CUDA(cudaMemcpyAsync(host, S.logits.p, (size_t)M.cfg.vocab * 4, cudaMemcpyDeviceToHost, S.stream));
   }
   FABER_CUDA(cudaStreamSynchronize(S.stream));
+  check_device_waits();
 }
 
 inline void run_position_logits(SessionState& S, float* host, uint64_t cap) {
@@ -835,6 +927,7 @@ inline void run_greedy(SessionState& S, uint32_t n_gen, const int64_t* eog, uint
   FABER_CUDA(cudaMemcpyAsync(out, S.gen.p, (size_t)n_gen * 8, cudaMemcpyDeviceToHost, S.stream));
   FABER_CUDA(cudaMemcpyAsync(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost, S.stream));
   FABER_CUDA(cudaStreamSynchronize(S.stream));
+  check_device_waits();
   if (!S.trace) FABER_CUDA(cudaEventElapsedTime(&S.last_greedy_ms, S.ev0, S.ev1));
   if (all_finite) *all_finite = st.finite;
   S.n += n_gen - 1;
@@ -988,7 +1081,11 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_reset(FaberGpuSession* s) {
     FABER_CUDA(cudaSetDevice(S.device));
     FABER_CUDA(cudaStreamSynchronize(S.stream));
     StepState st = {};
+    FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+    const uint32_t epoch = st.tp_epoch;  // exchange epochs never repeat
+    st = StepState{};
     st.finite = 1;
+    st.tp_epoch = epoch;
     FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
     S.n = 0;
     S.prefix_pending = false;

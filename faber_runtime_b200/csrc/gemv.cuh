@@ -42,14 +42,28 @@ namespace faber {
 
 // PRO_NORM_RES: x = x + x2 (the residual add deferred from a tensor-parallel
 // all-reduce), written back by CTA 0, then rms_norm as PRO_NORM.
-enum GemvPrologue : int { PRO_PLAIN = 0, PRO_NORM = 1, PRO_NORM_RES = 2 };
-enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+// PRO_NORM_PEERS: x_sum_out = x + (sum over ranks of the exchange buffer, in
+// rank order), each CTA summing one slice, then a grid barrier, then rms_norm
+// of x_sum_out. EPI_PEERS: the row-parallel output rows go to this rank's
+// slot in every rank's exchange buffer over NVLink. Each value travels with
+// its exchange epoch in one 8-byte store (single-copy atomic), so a reader
+// spins on the element itself: no fence, ticket or flag.
+enum GemvPrologue : int { PRO_PLAIN = 0, PRO_NORM = 1, PRO_NORM_RES = 2, PRO_NORM_PEERS = 3 };
+enum GemvEpilogue : int {
+  EPI_STORE = 0,
+  EPI_RESID = 1,
+  EPI_QKV = 2,
+  EPI_SWIGLU = 3,
+  EPI_LOGITS = 4,
+  EPI_PEERS = 5
+};
 enum GemvLayout : int { WL_TILED = 0, WL_NATIVE = 1, WL_F16 = 2 };
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kXPad = 256;  // zero halo (elements) in front of x for row offsets
 constexpr int kMaxEog = 8;
+constexpr int kMaxTp = 8;
 
 struct GemvArgs {
   const uint8_t* w;          // weights (layout per template parameter)
@@ -61,7 +75,7 @@ struct GemvArgs {
   const int32_t* row_map;    // [n_tiles*16] output row of each tile row (-1 pad), or null
   const float* x;            // input (PRO_PLAIN: the vector; PRO_NORM: the residual stream)
   const float* x2;           // PRO_NORM_RES: second residual term
-  float* x_sum_out;          // PRO_NORM_RES: x + x2 (CTA 0 writes)
+  float* x_sum_out;          // PRO_NORM_RES (CTA 0 writes) / PRO_NORM_PEERS (each CTA a slice): the summed input
   const float* norm_w;       // PRO_NORM weight
   float eps;
   float* x_norm_out;         // optional copy of the normalized input (CTA 0 writes)
@@ -82,7 +96,93 @@ struct GemvArgs {
   int32_t n_eog;
   int32_t row_offset;        // global index of local row 0 (vocab shard)
   int64_t eog[kMaxEog];
+  // tensor-parallel exchange over peer memory
+  int32_t tp;                          // ranks in the group
+  int32_t tp_stage;                    // this exchange within a step (2 * layer + 0 O / 1 down)
+  int32_t tp_stages;                   // exchanges per step
+  const uint32_t* epoch_ptr;           // steps taken (StepState), the epoch base
+  unsigned long long* peer_dst[kMaxTp];  // EPI_PEERS: this rank's slot in rank r's buffer
+  const unsigned long long* red;       // PRO_NORM_PEERS: local buffer [tp][n_cols]
+  unsigned int* grid_bar;              // PRO_NORM_PEERS: {arrived, generation} (local)
 };
+
+// Epoch of one exchange: unique per (step, exchange) and identical on every
+// rank (each rank's embed kernel counts the same steps).
+__device__ __forceinline__ uint32_t tp_epoch(const GemvArgs& a) {
+  return *a.epoch_ptr * (uint32_t)a.tp_stages + (uint32_t)a.tp_stage + 1u;
+}
+
+__device__ __forceinline__ void st_peer(unsigned long long* p, float v, uint32_t epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_peer(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+// Set by a kernel whose bounded wait expired (never in a correct run):
+// 1 = a pipeline stage, 2 = a tensor-parallel peer, 3 = a grid barrier. The
+// host reads and clears it after each step.
+__device__ int g_pipe_error;
+
+// One exchanged value once its epoch has arrived. Bounded: 2^20 polls (well
+// under a second), and no wait at all once an earlier wait has expired.
+constexpr uint32_t kPeerSpinLimit = 1u << 20;
+__device__ __forceinline__ float peer_value(const unsigned long long* p, uint32_t epoch) {
+  unsigned long long w = ld_peer(p);
+  for (uint32_t n = 0; (uint32_t)(w >> 32) != epoch; w = ld_peer(p)) {
+    if (++n == kPeerSpinLimit || ((n & 1023u) == 0 && *(volatile int*)&g_pipe_error)) {
+      atomicExch(&g_pipe_error, 2);
+      break;
+    }
+  }
+  return __uint_as_float((uint32_t)w);
+}
+
+// Sum of the ranks' partials of element i, in rank order. All ranks' words
+// are requested before any is checked (one round trip when they have
+// arrived); a word still carrying an older epoch is then waited for.
+__device__ __forceinline__ float peer_sum1(const GemvArgs& a, int i, uint32_t e) {
+  unsigned long long w[kMaxTp];
+#pragma unroll
+  for (int p = 0; p < kMaxTp; ++p)
+    if (p < a.tp) w[p] = ld_peer(a.red + (size_t)p * a.n_cols + i);
+  float s = 0.0f;
+#pragma unroll
+  for (int p = 0; p < kMaxTp; ++p) {
+    if (p >= a.tp) break;
+    const float v = (uint32_t)(w[p] >> 32) == e ? __uint_as_float((uint32_t)w[p])
+                                                : peer_value(a.red + (size_t)p * a.n_cols + i, e);
+    s = p == 0 ? v : s + v;
+  }
+  return s;
+}
+
+// Grid-wide barrier of a persistent grid (every CTA resident), thread 0 of
+// each CTA; sense-reversing, so the same two words serve every launch.
+// Bounded like the other waits.
+__device__ __forceinline__ void grid_barrier(unsigned int* bar) {
+  volatile unsigned int* gen = bar + 1;
+  const unsigned int my_gen = *gen;
+  __threadfence();
+  if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+    bar[0] = 0u;
+    __threadfence();
+    atomicAdd(bar + 1, 1u);
+    return;
+  }
+  for (uint32_t n = 0; *gen == my_gen; ++n) {
+    if (n == kPeerSpinLimit) {
+      atomicExch(&g_pipe_error, 3);
+      break;
+    }
+    __nanosleep(32);
+  }
+  __threadfence();
+}
 
 // Padded shared-memory index of virtual x element v (8 halves of padding
 // every 64 keeps the B-fragment reads of the four lane groups on distinct
@@ -148,6 +248,7 @@ __device__ __forceinline__ int split_shift(float bound) {
 // Element i of the GEMV input before normalization (x, or x + x2).
 template <int PRO>
 __device__ __forceinline__ float4 load_x4(const GemvArgs& a, int i4) {
+  if (PRO == PRO_NORM_PEERS) return __ldcg(reinterpret_cast<const float4*>(a.x_sum_out) + i4);
   float4 v = reinterpret_cast<const float4*>(a.x)[i4];
   if (PRO == PRO_NORM_RES) {
     const float4 u = reinterpret_cast<const float4*>(a.x2)[i4];
@@ -158,7 +259,9 @@ __device__ __forceinline__ float4 load_x4(const GemvArgs& a, int i4) {
 
 template <int PRO>
 __device__ __forceinline__ float load_x1(const GemvArgs& a, int i) {
-  return (PRO == PRO_NORM_RES) ? a.x[i] + a.x2[i] : a.x[i];
+  if (PRO == PRO_NORM_RES) return a.x[i] + a.x2[i];
+  if (PRO == PRO_NORM_PEERS) return __ldcg(a.x_sum_out + i);
+  return a.x[i];
 }
 
 // Normalized value: rms_norm's x*scale*w with two rounded products
@@ -195,6 +298,17 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
   constexpr int NT = kGemvThreads;
   const int n = a.n_cols;
   const int tid = threadIdx.x;
+  if (PRO == PRO_NORM_PEERS) {
+    // this CTA's slice of x + sum of the ranks' partials, then every slice
+    const uint32_t e = tp_epoch(a);
+    const int per = (n + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int i1 = min(n, ((int)blockIdx.x + 1) * per);
+    for (int i = (int)blockIdx.x * per + tid; i < i1; i += NT)
+      a.x_sum_out[i] = a.x[i] + peer_sum1(a, i, e);
+    cbar<NAMED>();
+    if (tid == 0) grid_barrier(a.grid_bar);
+    cbar<NAMED>();
+  }
   const bool vec = (n % 4 == 0) && aligned16(a.x) &&
                    (PRO == PRO_PLAIN || aligned16(a.norm_w)) &&
                    (PRO != PRO_NORM_RES || aligned16(a.x2));
@@ -687,6 +801,12 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, int p
   if (EPI == EPI_STORE) {
     if (v0) a.out[r0] = y0;
     if (v1) a.out[r1] = y1;
+  } else if (EPI == EPI_PEERS) {
+    const uint32_t e = tp_epoch(a);
+    for (int p = 0; p < a.tp; ++p) {
+      if (v0) st_peer(a.peer_dst[p] + r0, y0, e);
+      if (v1) st_peer(a.peer_dst[p] + r1, y1, e);
+    }
   } else if (EPI == EPI_RESID) {
     // residual_add (src/decoder_ops.rs:420-427)
     if (v0) a.out[r0] = a.res[r0] + y0;
@@ -835,9 +955,6 @@ constexpr int kPipeThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageBytes = kConsumerWarps * kTileItemBytes;  // 18 KB
 constexpr int kMaxStages = 4;
 constexpr uint32_t kSpinLimit = 1u << 20;
-
-// Set by a kernel whose bounded wait expired (never in a correct run).
-__device__ int g_pipe_error;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

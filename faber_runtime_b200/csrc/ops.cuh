@@ -103,7 +103,8 @@ struct StepState {
   int32_t gen_count;     // greedy tokens produced
   int32_t finite;        // finite gate over all logits since reset
   int32_t status;        // nonzero: a kernel-side check failed (token out of range)
-  int32_t pad;
+  uint32_t tp_epoch;     // steps taken since the session opened (kept by reset):
+                         // the epoch base of tensor-parallel exchanges
   unsigned long long argmax_key;
 };
 
@@ -123,6 +124,7 @@ __global__ void embed_kernel(StepState* st, const __half* __restrict__ embd, int
     st->cur_pos = st->n;
     st->n = st->n + 1;
     st->argmax_key = 0ull;
+    st->tp_epoch = st->tp_epoch + 1u;
   }
 }
 
