@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "prefill.cuh"
 
 namespace faber {
 
@@ -142,6 +143,9 @@ struct SessionState {
   // bytes each, then the consumers' grid-barrier words. Every rank maps every
   // other rank's buffer (CUDA IPC) and stores its partials there.
   DevBuf tp_buf;
+  // prompt pass scratch (allocated on first use, for up to kPrefillChunk tokens)
+  DevBuf pf_h, pf_xs, pf_scale, pf_q, pf_ctx, pf_act;
+  int pf_cap = 0;
   std::vector<unsigned char*> tp_base;  // rank r's buffer in this process
   DevBuf state;           // StepState
   DevBuf gen;             // int64 [max_ctx]
@@ -831,6 +835,191 @@ inline void check_prefix_complete(SessionState& S) {
   S.prefix_pending = false;
 }
 
+// ---------------------------------------------------------------------------
+// Prompt pass on the tensor cores: all tokens of a chunk through each layer
+// at once (the tcgen05 GEMMs of prefill.cuh), the same values as pushing
+// them one by one (src/cpu_oracle.rs:513-534 / 859-912).
+// ---------------------------------------------------------------------------
+constexpr int kPrefillChunk = 2048;
+constexpr uint64_t kPrefillMinTokens = 32;
+
+inline bool prefill_supported(const ModelState& M) {
+  const FaberModelConfigV1& c = M.cfg;
+  const uint32_t nq = (uint32_t)M.Hl * c.head_dim;
+  return M.tp == 1 && c.d_model % 256 == 0 && nq % 256 == 0 && M.Fl % 256 == 0;
+}
+
+using TmapEncode = PFN_cuTensorMapEncodeTiled_v12000;
+
+inline TmapEncode tmap_encoder() {
+  static TmapEncode fn = nullptr;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    FABER_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    require(p != nullptr && q == cudaDriverEntryPointSuccess, FABER_STATUS_UNSUPPORTED,
+            "cuTensorMapEncodeTiled is not available");
+    fn = reinterpret_cast<TmapEncode>(p);
+  }
+  return fn;
+}
+
+// Tensor map over the split activations [rows][K] f16: 64 x 256 boxes with the
+// 128-byte swizzle the UMMA B descriptor reads (rows past the end read 0).
+inline CUtensorMap xs_tensor_map(const __half* xs, uint64_t rows, uint64_t K) {
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {K, rows};
+  const cuuint64_t strides[1] = {K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kPgBK, (cuuint32_t)kPgBN};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = tmap_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(xs),
+                                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  require(r == CUDA_SUCCESS, FABER_STATUS_CUDA_ERROR,
+          "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return map;
+}
+
+template <int EPI>
+void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGemmArgs a, int n_tok,
+                         cudaStream_t stream) {
+  auto kern = prefill_gemm_kernel<EPI>;
+  static thread_local std::map<int, bool> attr_done;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPgSmemBytes));
+    attr_done[dev] = true;
+  }
+  require(W.identity, FABER_STATUS_UNSUPPORTED, "prefill GEMM needs whole super-block rows");
+  a.w = W.w.as<uint8_t>();
+  a.n_tiles = W.n_tiles;
+  a.nb = W.nb;
+  a.m_rows = W.rows;
+  a.n_tok = n_tok;
+  const dim3 grid((W.rows + kPgBM - 1) / kPgBM, (2 * n_tok + kPgBN - 1) / kPgBN);
+  prefill_gemm_kernel<EPI><<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, a);
+  FABER_CUDA(cudaGetLastError());
+}
+
+inline void ensure_prefill_scratch(SessionState& S, int cap) {
+  if (S.pf_cap >= cap) return;
+  ModelState& M = S.m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  const size_t d = c.d_model, nq = (size_t)M.Hl * c.head_dim, F = M.Fl;
+  const size_t kmax = std::max(d, std::max(nq, F));
+  S.pf_h.alloc((size_t)cap * d * 4);
+  S.pf_xs.alloc((size_t)2 * cap * kmax * 2);
+  S.pf_scale.alloc((size_t)cap * 4);
+  S.pf_q.alloc((size_t)cap * nq * 4);
+  S.pf_ctx.alloc((size_t)cap * nq * 4);
+  S.pf_act.alloc((size_t)cap * F * 4);
+  S.pf_cap = cap;
+}
+
+// Tokens [0, count) at positions S.n.. : every layer over the chunk, K/V into
+// the cache; afterwards the last token's residual is the session's h.
+inline void run_prefill(SessionState& S, const int64_t* dev_tokens, int count) {
+  ModelState& M = S.m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  const int d = (int)c.d_model, hd = (int)c.head_dim, nq = M.Hl * hd, nk = M.Hkvl * hd;
+  const int F = M.Fl;
+  const size_t layer_cache = (size_t)S.max_ctx * nk;
+  ensure_prefill_scratch(S, std::min(count, kPrefillChunk));
+  StepState* st = st_ptr(S);
+  for (int c0 = 0; c0 < count; c0 += kPrefillChunk) {
+    const int n = std::min(kPrefillChunk, count - c0);
+    const int pos0 = (int)S.n + c0;
+    float* H = S.pf_h.as<float>();
+    __half* xs = S.pf_xs.as<__half>();
+    float* xscale = S.pf_scale.as<float>();
+    const CUtensorMap map_d = xs_tensor_map(xs, 2 * (uint64_t)n, d);
+    const CUtensorMap map_q = xs_tensor_map(xs, 2 * (uint64_t)n, nq);
+    const CUtensorMap map_f = xs_tensor_map(xs, 2 * (uint64_t)n, F);
+    prefill_embed_kernel<<<n, 256, 0, S.stream>>>(dev_tokens + c0, M.embd_f16.as<__half>(), d,
+                                                  (int)c.vocab, H, &st->status);
+    FABER_CUDA(cudaGetLastError());
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+      LayerDev& L = M.layers[l];
+      // attention block
+      prefill_split_kernel<true><<<n, kGemvThreads, 0, S.stream>>>(H, d, L.attn_norm.as<float>(),
+                                                                   c.rms_eps, xs, xscale);
+      {
+        PrefillGemmArgs a = {};
+        a.xscale = xscale;
+        a.q_out = S.pf_q.as<float>();
+        a.k_cache = S.kcache.as<__half>() + l * layer_cache;
+        a.v_cache = S.vcache.as<__half>() + l * layer_cache;
+        a.rope = S.rope.as<float2>();
+        a.nq = nq;
+        a.nk = nk;
+        a.head_dim = hd;
+        a.pos0 = pos0;
+        launch_prefill_gemm<PG_QKV>(L.qkv, map_d, a, n, S.stream);
+      }
+      {
+        const dim3 grid(M.Hl, (n + 15) / 16);
+        const float scale = 1.0f / sqrtf((float)hd);
+        if (hd == 128)
+          prefill_attention_kernel<128><<<grid, 128, 0, S.stream>>>(
+              S.pf_q.as<float>(), S.kcache.as<__half>() + l * layer_cache,
+              S.vcache.as<__half>() + l * layer_cache, S.pf_ctx.as<float>(), n, pos0, M.Hl, M.Hkvl, scale);
+        else
+          prefill_attention_kernel<64><<<grid, 128, 0, S.stream>>>(
+              S.pf_q.as<float>(), S.kcache.as<__half>() + l * layer_cache,
+              S.vcache.as<__half>() + l * layer_cache, S.pf_ctx.as<float>(), n, pos0, M.Hl, M.Hkvl, scale);
+        FABER_CUDA(cudaGetLastError());
+      }
+      prefill_split_kernel<false><<<n, kGemvThreads, 0, S.stream>>>(S.pf_ctx.as<float>(), nq, nullptr,
+                                                                    0.0f, xs, xscale);
+      {
+        PrefillGemmArgs a = {};
+        a.xscale = xscale;
+        a.out = H;
+        a.ld_out = d;
+        launch_prefill_gemm<PG_RESID>(L.o, map_q, a, n, S.stream);
+      }
+      // feed-forward block
+      prefill_split_kernel<true><<<n, kGemvThreads, 0, S.stream>>>(H, d, L.ffn_norm.as<float>(),
+                                                                   c.rms_eps, xs, xscale);
+      {
+        PrefillGemmArgs a = {};
+        a.xscale = xscale;
+        a.out = S.pf_act.as<float>();
+        a.ld_out = F;
+        launch_prefill_gemm<PG_SWIGLU>(L.gateup, map_d, a, n, S.stream);
+      }
+      prefill_split_kernel<false><<<n, kGemvThreads, 0, S.stream>>>(S.pf_act.as<float>(), F, nullptr,
+                                                                    0.0f, xs, xscale);
+      {
+        PrefillGemmArgs a = {};
+        a.xscale = xscale;
+        a.out = H;
+        a.ld_out = d;
+        launch_prefill_gemm<PG_RESID>(L.down, map_f, a, n, S.stream);
+      }
+      FABER_CUDA(cudaGetLastError());
+    }
+    if (c0 + n == count) {
+      // the decode state continues from the last prompt token
+      FABER_CUDA(cudaMemcpyAsync(S.h.p, H + (size_t)(n - 1) * d, (size_t)d * 4,
+                                 cudaMemcpyDeviceToDevice, S.stream));
+    }
+  }
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  check_device_waits();
+  StepState hs;
+  FABER_CUDA(cudaMemcpy(&hs, S.state.p, sizeof(hs), cudaMemcpyDeviceToHost));
+  require(hs.status == 0, FABER_STATUS_KERNEL_ERROR, "device-side token check failed");
+  hs.cur_pos = (int32_t)(S.n + (uint64_t)count - 1);
+  hs.n = (int32_t)(S.n + (uint64_t)count);
+  FABER_CUDA(cudaMemcpy(S.state.p, &hs, sizeof(hs), cudaMemcpyHostToDevice));
+  S.n += (uint64_t)count;
+}
+
 inline void run_push(SessionState& S, const int64_t* tokens, uint64_t count) {
   ModelState& M = S.m->s;
   FABER_CUDA(cudaSetDevice(S.device));
@@ -842,6 +1031,10 @@ inline void run_push(SessionState& S, const int64_t* tokens, uint64_t count) {
   require(S.n + count <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
   if (count == 0) return;
   FABER_CUDA(cudaMemcpyAsync(S.prompt.p, tokens, count * 8, cudaMemcpyHostToDevice, S.stream));
+  if (!S.trace && count >= kPrefillMinTokens && prefill_supported(M)) {
+    run_prefill(S, S.prompt.as<int64_t>(), (int)count);
+    return;
+  }
   if (S.trace) {
     for (uint64_t i = 0; i < count; ++i) {
       FABER_CUDA(cudaMemcpyAsync(&st_ptr(S)->input_token, S.prompt.as<int64_t>() + i, 8,

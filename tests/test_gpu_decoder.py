@@ -171,6 +171,34 @@ def test_7b_shape_two_layers_over_prefix(cuda):
     assert len(drun) == n_prefix + 4
 
 
+PREFILL_CASES = [
+    # (model, prompt length): the prompt goes through the tensor-core prompt
+    # pass (tcgen05 GEMMs, batched causal attention) in chunks of 2048
+    ("7b-width-2-layers", 300),
+    ("gqa-small", 2100),  # two chunks: the second attends to the first's cache
+]
+
+
+@pytest.mark.parametrize("which,n_prompt", PREFILL_CASES)
+def test_prompt_pass_matches_oracle(cuda, which, n_prompt):
+    import oracle as o
+    from faber_runtime_b200 import LLAMA2_7B, ForwardRun, ModelConfig, synth
+    if which == "gqa-small":
+        cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=4, head_dim=64,
+                          ffn=2816, vocab=4096, tied_head=False, rope_theta=500000.0,
+                          name="prefill-gqa")
+    else:
+        cfg = LLAMA2_7B.with_layers(2)
+    om, dm, _ = build_pair(cfg, 91, norms="random")
+    prompt = synth.tokens(91, 4, n_prompt, cfg.vocab)
+    ref_tokens, ref_logits, _ = om.greedy(prompt, 4, want_logits=True)
+    run = ForwardRun(dm, prompt, context_length=n_prompt + 8)
+    assert len(run) == n_prompt
+    within(run.position_logits(), ref_logits[0])
+    toks, fin = run.greedy(4)
+    assert fin and toks.tolist() == ref_tokens.tolist()
+
+
 def test_fail_closed_and_commit_contract(tiny):
     from faber_runtime_b200 import FaberError, ForwardRun, OracleError
     _, dm, _ = tiny
