@@ -18,10 +18,11 @@
 //   * warp 1: allocates 256 TMEM columns, and lane 0 issues
 //     tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256, K 16) from the two
 //     shared-memory descriptors, committing each stage back to its mbarrier;
-//   * warps 2-5 (one per TMEM lane quadrant): dequantize 128 rows x 64
-//     weights per stage with the GEMV's exact f16 formation, write them in the
-//     128-byte-swizzled K-major layout the A descriptor reads, and finally
-//     read the accumulators (tcgen05.ld) for the epilogue.
+//   * warps 2-9 (two per TMEM lane quadrant): dequantize 128 rows x 64
+//     weights per stage (a thread makes one row's low- or high-nibble half)
+//     with the GEMV's exact f16 formation, write them in the 128-byte-swizzled
+//     K-major layout the A descriptor reads, and finally read the
+//     accumulators (tcgen05.ld) for the epilogue.
 // Every wait is bounded (g_pipe_error = 1 on expiry, then the CTA proceeds;
 // barriers stay balanced).
 #pragma once
@@ -37,7 +38,8 @@ constexpr int kPgBM = 128;
 constexpr int kPgBN = 256;
 constexpr int kPgBK = 64;
 constexpr int kPgStages = 3;
-constexpr int kPgThreads = 192;
+constexpr int kPgThreads = 320;  // warp 0 loads, warp 1 MMA, warps 2-9 dequant + epilogue
+constexpr int kPgDequantWarps = 8;
 constexpr int kPgATile = kPgBM * kPgBK * 2;                         // 16 KB
 constexpr int kPgBTile = kPgBN * kPgBK * 2;                         // 32 KB
 constexpr int kPgRaw = (kPgBM / kTileRows) * kTileItemBytes;        // 18 KB
@@ -139,16 +141,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 64 consecutive k of one weight row (the thread's own row) into the
-// 128-byte-swizzled A tile: chunk c of row r lands at chunk c ^ (r & 7).
-__device__ __forceinline__ void store_a_row(uint8_t* a_tile, int r, const uint32_t (&h)[32]) {
-  uint8_t* row = a_tile + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
-        make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
-}
-
 // ---- the kernel -----------------------------------------------------------
 template <int EPI>
 __global__ void __launch_bounds__(kPgThreads, 1)
@@ -174,12 +166,12 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPgStages; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&a_full[s], 4);
+      mbar_init(&a_full[s], kPgDequantWarps);
       mbar_init(&s_done[s], 1);
     }
     for (int r = 0; r < 2; ++r) {
       mbar_init(&raw_full[r], 1);
-      mbar_init(&raw_empty[r], 4);
+      mbar_init(&raw_empty[r], kPgDequantWarps);
     }
     mbar_init(tile_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -235,9 +227,12 @@ __global__ void __launch_bounds__(kPgThreads, 1)
       umma_commit(tile_done);
     }
   } else {
-    // dequant: thread i of warps 2-5 owns weight row i of the tile
+    // dequant: thread i of warps 2-9 owns weight row i % 128 of the tile, the
+    // low-nibble half (k 0..31 of the step, warps 2-5) or the high-nibble half
+    // (k 32..63, warps 6-9): two dequantizing warps per scheduler
     const int i = threadIdx.x - 64;
-    const int q_in_tile = i >> 4, row16 = i & 15;
+    const int row = i & (kPgBM - 1), half = i >> 7;
+    const int q_in_tile = row >> 4, row16 = row & 15;
     LaneConst lc;
     asm("mov.b32 %0, 0x64006400;" : "=r"(lc.m1024));
     asm("mov.b32 %0, 0x54005400;" : "=r"(lc.m64));
@@ -255,18 +250,32 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
       }
       const RowScales3 sc = row_scales3(hdr, chunk, lc);
-      uint32_t h[32];  // 64 f16: k 0..31 low nibbles (sub-block 2c), 32..63 high (2c+1)
+      // this half's scale constants: sub-block 2c (low nibbles) or 2c + 1
+      const uint32_t sc2 = half ? sc.schi2 : sc.sclo2, c2 = half ? sc.chi2 : sc.clo2;
+      const float nm = half ? sc.nm2 : sc.nm1;
+      uint32_t h[16];  // 32 f16: k 32 * half + 0..31
 #pragma unroll
       for (int wd = 0; wd < 8; ++wd) {
         const uint32_t w = word_of(wd < 4 ? q0 : q1, wd & 3);
-        uint32_t lo0, lo2, hi0, hi2;  // (k0,k2), (k1,k3) pairs of bytes 4wd..4wd+3
-        dequant_word3(w, sc, lc, lo0, lo2, hi0, hi2);
-        h[2 * wd] = prmt<0x5410>(lo0, lo2);
-        h[2 * wd + 1] = prmt<0x7632>(lo0, lo2);
-        h[16 + 2 * wd] = prmt<0x5410>(hi0, hi2);
-        h[16 + 2 * wd + 1] = prmt<0x7632>(hi0, hi2);
+        const uint32_t u = w >> 8;
+        // (k0, k2) from bytes 0/2 and (k1, k3) from bytes 1/3 of the word
+        const uint32_t p02 = half ? hfma2_u(and_or<0x00f000f0u>(w, lc.m64), sc2, c2)
+                                  : hfma2_u(and_or<0x000f000fu>(w, lc.m1024), sc2, c2);
+        const uint32_t p13 = half ? hfma2_u(and_or<0x00f000f0u>(u, lc.m64), sc2, c2)
+                                  : hfma2_u(and_or<0x000f000fu>(u, lc.m1024), sc2, c2);
+        const float2 a02 = mixed_fma_pair(p02, sc.dword, nm);
+        const float2 a13 = mixed_fma_pair(p13, sc.dword, nm);
+        const uint32_t v02 = pack_half2(a02.x, a02.y), v13 = pack_half2(a13.x, a13.y);
+        h[2 * wd] = prmt<0x5410>(v02, v13);      // (k0, k1)
+        h[2 * wd + 1] = prmt<0x7632>(v02, v13);  // (k2, k3)
       }
-      store_a_row(sa + s * kPgATile, i, h);
+      {
+        uint8_t* arow = sa + s * kPgATile + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          *reinterpret_cast<uint4*>(arow + (((4 * half + cc) ^ (row & 7)) << 4)) =
+              make_uint4(h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
+      }
       // generic-proxy writes become visible to the tensor core's async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -275,12 +284,14 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         if (chunk == 3) mbar_arrive(&raw_empty[r]);
       }
     }
-    // epilogue: this warp's TMEM lane quadrant = rows 32 * (warp % 4) ..
+    // epilogue: this warp's TMEM lane quadrant = rows 32 * (warp % 4) ..,
+    // columns split between the two warps of a quadrant
     mbar_wait(tile_done, 0);
     tc_fence_after();
     const int quad = warp & 3;
     const int m = m_tile * kPgBM + quad * 32 + lane;
-    for (int c0 = 0; c0 < kPgBN; c0 += 32) {
+    const int cbeg = half * (kPgBN / 2);
+    for (int c0 = cbeg; c0 < cbeg + kPgBN / 2; c0 += 32) {
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
 #pragma unroll
