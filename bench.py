@@ -5,7 +5,7 @@ Workload (default): Llama-2-7B-shape decoder (32 layers, d 4096, 32 heads x
 128, SwiGLU 11008, vocab 32000, RMSNorm eps 1e-5, RoPE theta 1e4), every
 linear Q4_K with seeded random fields, f32 N(0, 0.02) token embedding and
 output norm, batch 1. The KV cache is filled by the prompt pass over 2048
-random token ids (tcgen05 GEMMs and batched causal attention on one GPU; token
+random token ids (tcgen05 GEMMs and tensor-core flash attention on one GPU; token
 by token under tensor parallelism), then W warm-up and K timed greedy tokens
 run as CUDA-graph replays.
 
@@ -314,7 +314,7 @@ def run_faber(args):
     run = ForwardRun(model, context_length=ctx)
     prompt = synth.tokens(SEED, 1, PREFILL, cfg.vocab)
     run.push_tokens(prompt)  # first prompt pass: scratch allocation, kernel set-up
-    # timed prompt pass (tcgen05 GEMMs + batched attention) on a reset session
+    # timed prompt pass (tcgen05 GEMMs + flash attention) on a reset session
     run.reset()
     torch.cuda.synchronize()
     if pg:

@@ -905,6 +905,26 @@ void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGe
   FABER_CUDA(cudaGetLastError());
 }
 
+// Causal attention of a prompt block (queries in pf_q, keys and values of
+// positions 0 .. pos0 + n - 1 in this layer's cache) into pf_ctx.
+template <int HD>
+void launch_prefill_flash(SessionState& S, size_t cache_off, int n, int pos0, float scale) {
+  ModelState& M = S.m->s;
+  auto kern = prefill_flash_kernel<HD>;
+  static thread_local std::map<int, bool> attr_done;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem_bytes<HD>()));
+    attr_done[dev] = true;
+  }
+  const dim3 grid(M.Hl, (n + kFaQ - 1) / kFaQ);
+  kern<<<grid, kFaThreads, fa_smem_bytes<HD>(), S.stream>>>(
+      S.pf_q.as<float>(), S.kcache.as<__half>() + cache_off, S.vcache.as<__half>() + cache_off,
+      S.pf_ctx.as<float>(), n, pos0, M.Hl, M.Hkvl, scale);
+  FABER_CUDA(cudaGetLastError());
+}
+
 inline void ensure_prefill_scratch(SessionState& S, int cap) {
   if (S.pf_cap >= cap) return;
   ModelState& M = S.m->s;
@@ -961,17 +981,11 @@ inline void run_prefill(SessionState& S, const int64_t* dev_tokens, int count) {
         launch_prefill_gemm<PG_QKV>(L.qkv, map_d, a, n, S.stream);
       }
       {
-        const dim3 grid(M.Hl, (n + 15) / 16);
         const float scale = 1.0f / sqrtf((float)hd);
         if (hd == 128)
-          prefill_attention_kernel<128><<<grid, 128, 0, S.stream>>>(
-              S.pf_q.as<float>(), S.kcache.as<__half>() + l * layer_cache,
-              S.vcache.as<__half>() + l * layer_cache, S.pf_ctx.as<float>(), n, pos0, M.Hl, M.Hkvl, scale);
+          launch_prefill_flash<128>(S, l * layer_cache, n, pos0, scale);
         else
-          prefill_attention_kernel<64><<<grid, 128, 0, S.stream>>>(
-              S.pf_q.as<float>(), S.kcache.as<__half>() + l * layer_cache,
-              S.vcache.as<__half>() + l * layer_cache, S.pf_ctx.as<float>(), n, pos0, M.Hl, M.Hkvl, scale);
-        FABER_CUDA(cudaGetLastError());
+          launch_prefill_flash<64>(S, l * layer_cache, n, pos0, scale);
       }
       prefill_split_kernel<false><<<n, kGemvThreads, 0, S.stream>>>(S.pf_ctx.as<float>(), nq, nullptr,
                                                                     0.0f, xs, xscale);

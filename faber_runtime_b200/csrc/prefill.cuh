@@ -399,138 +399,278 @@ __global__ void __launch_bounds__(kGemvThreads) prefill_split_kernel(const float
   if (threadIdx.x == 0) xscale[t] = ldexpf(1.0f, s);
 }
 
-// Sum over the warp of 32 per-lane values; lane l returns the total of value
-// l (levels pair lanes differing in bit 4, 3, 2, 1, 0).
-__device__ __forceinline__ float butterfly32(float (&p)[32], int lane) {
-#pragma unroll
-  for (int level = 0; level < 5; ++level) {
-    const int half = 16 >> level;
-    const bool upper = (lane & half) != 0;
-#pragma unroll
-    for (int i = 0; i < half; ++i) {
-      const float keep = upper ? p[i + half] : p[i];
-      const float send = upper ? p[i] : p[i + half];
-      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
-    }
-  }
-  return p[0];
+// ---- causal attention of a prompt block on the tensor cores -----------------
+//
+// attention_gqa (src/cpu_oracle.rs:711-792) for a block of n queries at
+// positions pos0 .. pos0 + n - 1 over the f16 K/V cache (positions 0 ..
+// pos0 + n - 1, this block's rows already written by the QKV GEMM). Query
+// row t of head h attends to the keys 0 .. pos0 + t of kv head h / ratio.
+//
+// CTA = (head, 64 queries), 4 warps of 16 queries; keys in tiles of 64,
+// double-buffered in shared memory by cp.async (rows past the block's last
+// key are zero-filled). Both products run on mma.sync m16n8k16 (f16 in, f32
+// accumulate) with f32-faithful operands:
+//   * each query row is scaled by a power of two 2^-s and split exactly,
+//     q * 2^-s = qh + ql (two f16), so S = (qh + ql) K^T carries ~22 bits;
+//     the K rows are f16 in the cache, so every product is exact;
+//   * the probabilities p = exp(s - m) in [0, 1] are split p = ph + pl the
+//     same way for O += (ph + pl) V.
+// The softmax is the online (running max and sum) form; the result is O / l.
+// Shared-memory rows are HD halfs with 16-byte chunks XOR-swizzled by the
+// row's low three bits, so every ldmatrix phase touches 32 distinct banks.
+constexpr int kFaQ = 64;
+constexpr int kFaK = 64;
+constexpr int kFaThreads = 128;
+
+template <int HD>
+__host__ __device__ constexpr int fa_tile_bytes() { return kFaK * HD * 2; }
+// Qhi, Qlo (64 rows each), then two stages of (K, V)
+template <int HD>
+__host__ __device__ constexpr int fa_smem_bytes() { return 2 * kFaQ * HD * 2 + 4 * fa_tile_bytes<HD>(); }
+
+template <int HD>
+__device__ __forceinline__ uint32_t fa_off(int row, int chunk) {
+  return (uint32_t)(row * HD * 2 + ((chunk ^ (row & 7)) << 4));
 }
 
-// Causal GQA attention of a prompt block (attention_gqa, src/cpu_oracle.rs:
-// 711-792): query t of the block sits at position pos0 + t and attends to the
-// cached positions 0..pos0 + t (kv head h / ratio). CTA = (head, 16 queries),
-// 4 warps of 4 queries; lanes own head_dim / 32 dims. Keys go 8 at a time:
-// per-lane partial dots of 4 queries x 8 keys, a 32-value butterfly leaves
-// lane l with the score of (query l >> 3, key l & 7); then an online softmax
-// per query (every lane keeps all 4 queries' max and sum) and the p * V
-// update with p broadcast by shuffles. scale = 1 / sqrt(head_dim).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// D += A(16x16 f16, row) * B(16x8 f16, col), f32 accumulate
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+// exact two-term split of (x, y): hi = f16(x, y), lo = f16 of the remainders
+__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  hi = h2_bits(h);
+  lo = h2_bits(__floats2half2_rn(x - __low2float(h), y - __high2float(h)));
+}
+
 template <int HD>
-__global__ void __launch_bounds__(128) prefill_attention_kernel(const float* q, const __half* kc,
-                                                                const __half* vc, float* ctx,
-                                                                int n, int pos0, int n_heads,
-                                                                int n_kv_heads, float scale) {
-  constexpr int DPL = HD / 32;
-  const int h = blockIdx.x, q0 = blockIdx.y * 16;
+__global__ void __launch_bounds__(kFaThreads) prefill_flash_kernel(const float* q, const __half* kc,
+                                                                   const __half* vc, float* ctx,
+                                                                   int n, int pos0, int n_heads,
+                                                                   int n_kv_heads, float scale) {
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(128) unsigned char fa_smem[];
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(fa_smem);
+  const uint32_t qh_base = sbase, ql_base = sbase + kFaQ * HD * 2;
+  const uint32_t kv_base = sbase + 2 * kFaQ * HD * 2;  // stage s: K at +2s tiles, V at +2s+1
+  const int h = blockIdx.x;
+  const int qb = gridDim.y - 1 - blockIdx.y;  // the longest (causal) blocks start first
+  const int q0 = qb * kFaQ;
   const int kh = h / (n_heads / n_kv_heads);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t kvs = (size_t)n_kv_heads * HD, qstride = (size_t)n_heads * HD;
-  const size_t col = (size_t)kh * HD + lane * DPL;
-  float qv[4][DPL], m[4], l[4], acc[4][DPL];
-  int qpos[4];
+  const int kv_end = pos0 + min(n, q0 + kFaQ);  // keys [0, kv_end) are read
+  const int nkb = (kv_end + kFaK - 1) / kFaK;
+  const __half* kh_k = kc + (size_t)kh * HD;
+  const __half* kh_v = vc + (size_t)kh * HD;
+
+  auto load_tile = [&](int kb, int stage) {
+    const uint32_t kdst = kv_base + (uint32_t)(2 * stage) * fa_tile_bytes<HD>();
+    const uint32_t vdst = kdst + fa_tile_bytes<HD>();
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = q0 + warp * 4 + i;
-    qpos[i] = t < n ? pos0 + t : -1;  // -1: no query (every key masked)
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) {
-      qv[i][d] = t < n ? q[(size_t)t * qstride + (size_t)h * HD + lane * DPL + d] : 0.0f;
-      acc[i][d] = 0.0f;
+    for (int i = 0; i < kFaK * CH / kFaThreads; ++i) {
+      const int c = tid + i * kFaThreads;
+      const int row = c / CH, ch = c % CH;
+      const int key = kb * kFaK + row;
+      const bool valid = key < kv_end;
+      const size_t off = (size_t)(valid ? key : 0) * kvs + (size_t)ch * 8;
+      cp_async16(kdst + fa_off<HD>(row, ch), kh_k + off, valid);
+      cp_async16(vdst + fa_off<HD>(row, ch), kh_v + off, valid);
     }
-    m[i] = -INFINITY;
-    l[i] = 0.0f;
-  }
-  const int last = max(max(qpos[0], qpos[1]), max(qpos[2], qpos[3]));
-  const int qi = lane >> 3, kk = lane & 7;
-  for (int j0 = 0; j0 <= last; j0 += 8) {
-    float kf[8][DPL];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const bool in = j0 + k <= last;
-#pragma unroll
-      for (int d = 0; d < DPL; d += 2) {
-        float2 f = make_float2(0.0f, 0.0f);
-        if (in) f = __half22float2(*reinterpret_cast<const __half2*>(kc + (size_t)(j0 + k) * kvs + col + d));
-        kf[k][d] = f.x;
-        kf[k][d + 1] = f.y;
+    cp_async_commit();
+  };
+  load_tile(0, 0);
+
+  // Q rows of this warp: power-of-two scale per row, exact hi/lo split
+  int s_row0 = 0, s_row1 = 0;
+  {
+    constexpr int PL = HD / 32;  // values per lane
+    for (int r = 0; r < 16; ++r) {
+      const int row = warp * 16 + r, t = q0 + row;
+      float v[PL];
+      const float* src = q + (size_t)t * qstride + (size_t)h * HD + lane * PL;
+      if constexpr (PL == 4) {
+        const float4 f = t < n ? *reinterpret_cast<const float4*>(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[0] = f.x;
+        v[1] = f.y;
+        v[2] = f.z;
+        v[3] = f.w;
+      } else {
+        const float2 f = t < n ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
+        v[0] = f.x;
+        v[1] = f.y;
       }
-    }
-    float p[32];
+      float mx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < PL; ++i) mx = fmaxf(mx, fabsf(v[i]));
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        float s = 0.0f;
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const int s = split_shift(mx);
+      const float in_s = ldexpf(1.0f, -s);
+      if (r == (lane >> 2)) s_row0 = s;
+      if (r == (lane >> 2) + 8) s_row1 = s;
+      uint32_t hb[PL / 2], lb[PL / 2];
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) s = fmaf(qv[i][d], kf[k][d], s);
-        p[i * 8 + k] = s;
-      }
-    const float dot = butterfly32(p, lane);
-    int my_pos = qpos[0];
-#pragma unroll
-    for (int i = 1; i < 4; ++i) my_pos = qi == i ? qpos[i] : my_pos;
-    const bool valid = j0 + kk <= my_pos;
-    const float sc = valid ? dot * scale : -INFINITY;
-    float gm = sc;
-    gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
-    gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
-    gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 4));
-    float mn[4], c[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      mn[i] = fmaxf(m[i], __shfl_sync(0xffffffffu, gm, 8 * i));
-      c[i] = mn[i] == -INFINITY ? 1.0f : expf(m[i] - mn[i]);
-    }
-    float my_mn = mn[0];
-#pragma unroll
-    for (int i = 1; i < 4; ++i) my_mn = qi == i ? mn[i] : my_mn;
-    const float e = valid ? expf(sc - my_mn) : 0.0f;
-    float es = e;
-    es += __shfl_xor_sync(0xffffffffu, es, 1);
-    es += __shfl_xor_sync(0xffffffffu, es, 2);
-    es += __shfl_xor_sync(0xffffffffu, es, 4);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      l[i] = fmaf(l[i], c[i], __shfl_sync(0xffffffffu, es, 8 * i));
-      m[i] = mn[i];
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) acc[i][d] *= c[i];
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float vf[DPL];
-      const bool in = j0 + k <= last;
-#pragma unroll
-      for (int d = 0; d < DPL; d += 2) {
-        float2 f = make_float2(0.0f, 0.0f);
-        if (in) f = __half22float2(*reinterpret_cast<const __half2*>(vc + (size_t)(j0 + k) * kvs + col + d));
-        vf[d] = f.x;
-        vf[d + 1] = f.y;
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float pik = __shfl_sync(0xffffffffu, e, 8 * i + k);
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(pik, vf[d], acc[i][d]);
+      for (int i = 0; i < PL / 2; ++i) split2(v[2 * i] * in_s, v[2 * i + 1] * in_s, hb[i], lb[i]);
+      // element d = lane * PL sits in chunk d / 8 at byte (d % 8) * 2
+      const uint32_t o = fa_off<HD>(row, (lane * PL) / 8) + (uint32_t)((lane * PL) % 8) * 2;
+      if constexpr (PL == 4) {
+        asm volatile("st.shared.v2.b32 [%0], {%1,%2};\n" ::"r"(qh_base + o), "r"(hb[0]), "r"(hb[1]));
+        asm volatile("st.shared.v2.b32 [%0], {%1,%2};\n" ::"r"(ql_base + o), "r"(lb[0]), "r"(lb[1]));
+      } else {
+        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(qh_base + o), "r"(hb[0]));
+        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(ql_base + o), "r"(lb[0]));
       }
     }
   }
+  const float f0 = ldexpf(scale, s_row0), f1 = ldexpf(scale, s_row1);
+  // query positions of this thread's two accumulator rows, and the last key each may see
+  const int t0 = q0 + warp * 16 + (lane >> 2);
+  const int lim0 = min(pos0 + t0, kv_end - 1), lim1 = min(pos0 + t0 + 8, kv_end - 1);
+  const int warp_min_lim = min(pos0 + q0 + warp * 16, kv_end - 1);
+
+  float o_acc[HD / 8][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = q0 + warp * 4 + i;
-    if (t >= n) continue;
+  for (int i = 0; i < HD / 8; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  const int mi = lane >> 3, r8 = lane & 7;
+
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int stage = kb & 1;
+    if (kb + 1 < nkb) {
+      load_tile(kb + 1, stage ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t kbase = kv_base + (uint32_t)(2 * stage) * fa_tile_bytes<HD>();
+    const uint32_t vbase = kbase + fa_tile_bytes<HD>();
+    // S = Q K^T: 8 tiles of 16 queries x 8 keys
+    float sacc[8][4];
 #pragma unroll
-    for (int d = 0; d < DPL; ++d)
-      ctx[(size_t)t * qstride + (size_t)h * HD + lane * DPL + d] = acc[i][d] / l[i];
+    for (int i = 0; i < 8; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      uint32_t ah[4], al[4];
+      const uint32_t qo = fa_off<HD>(warp * 16 + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1));
+      ldsm_x4(qh_base + qo, ah);
+      ldsm_x4(ql_base + qo, al);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b[4];
+        ldsm_x4(kbase + fa_off<HD>(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
+        mma16816(sacc[2 * np], ah, b[0], b[1]);
+        mma16816(sacc[2 * np], al, b[0], b[1]);
+        mma16816(sacc[2 * np + 1], ah, b[2], b[3]);
+        mma16816(sacc[2 * np + 1], al, b[2], b[3]);
+      }
+    }
+    // scale, mask, online softmax (rows r = lane/4 and r + 8; 4 lanes per row)
+    const bool need_mask = kb * kFaK + kFaK - 1 > warp_min_lim;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = kb * kFaK + nt * 8 + 2 * (lane & 3) + e;
+        float a = sacc[nt][e] * f0, b = sacc[nt][2 + e] * f1;
+        if (need_mask) {
+          a = key <= lim0 ? a : -INFINITY;
+          b = key <= lim1 ? b : -INFINITY;
+        }
+        sacc[nt][e] = a;
+        sacc[nt][2 + e] = b;
+        mx0 = fmaxf(mx0, a);
+        mx1 = fmaxf(mx1, b);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float base0 = mn0 == -INFINITY ? 0.0f : mn0, base1 = mn1 == -INFINITY ? 0.0f : mn1;
+    const float c0 = expf(m0 - base0), c1 = expf(m1 - base1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sacc[nt][e] = expf(sacc[nt][e] - base0);
+        sacc[nt][2 + e] = expf(sacc[nt][2 + e] - base1);
+        ps0 += sacc[nt][e];
+        ps1 += sacc[nt][2 + e];
+      }
+    }
+    l0 = fmaf(l0, c0, ps0);
+    l1 = fmaf(l1, c1, ps1);
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) {
+      o_acc[i][0] *= c0;
+      o_acc[i][1] *= c0;
+      o_acc[i][2] *= c1;
+      o_acc[i][3] *= c1;
+    }
+    // O += P V: P from the S tiles (2j, 2j+1) as the A operand of key step j
+#pragma unroll
+    for (int j = 0; j < kFaK / 16; ++j) {
+      uint32_t ph[4], pl[4];
+      split2(sacc[2 * j][0], sacc[2 * j][1], ph[0], pl[0]);
+      split2(sacc[2 * j][2], sacc[2 * j][3], ph[1], pl[1]);
+      split2(sacc[2 * j + 1][0], sacc[2 * j + 1][1], ph[2], pl[2]);
+      split2(sacc[2 * j + 1][2], sacc[2 * j + 1][3], ph[3], pl[3]);
+#pragma unroll
+      for (int dp = 0; dp < HD / 16; ++dp) {
+        uint32_t b[4];
+        ldsm_x4_t(vbase + fa_off<HD>(16 * j + (mi & 1) * 8 + r8, 2 * dp + (mi >> 1)), b);
+        mma16816(o_acc[2 * dp], ph, b[0], b[1]);
+        mma16816(o_acc[2 * dp], pl, b[0], b[1]);
+        mma16816(o_acc[2 * dp + 1], ph, b[2], b[3]);
+        mma16816(o_acc[2 * dp + 1], pl, b[2], b[3]);
+      }
+    }
+    __syncthreads();  // the next iteration's load overwrites this stage
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+  float* out0 = ctx + (size_t)t0 * qstride + (size_t)h * HD + 2 * (lane & 3);
+  float* out1 = out0 + 8 * qstride;
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) {
+    if (t0 < n) *reinterpret_cast<float2*>(out0 + 8 * i) = make_float2(o_acc[i][0] * inv0, o_acc[i][1] * inv0);
+    if (t0 + 8 < n) *reinterpret_cast<float2*>(out1 + 8 * i) = make_float2(o_acc[i][2] * inv1, o_acc[i][3] * inv1);
   }
 }
 

@@ -173,7 +173,7 @@ def test_7b_shape_two_layers_over_prefix(cuda):
 
 PREFILL_CASES = [
     # (model, prompt length): the prompt goes through the tensor-core prompt
-    # pass (tcgen05 GEMMs, batched causal attention) in chunks of 2048
+    # pass (tcgen05 GEMMs, tensor-core flash attention) in chunks of 2048
     ("7b-width-2-layers", 300),
     ("gqa-small", 2100),  # two chunks: the second attends to the first's cache
 ]
