@@ -184,3 +184,46 @@ def test_two_gloo_ranks_reproduce_the_unsharded_step(faber, oracle):
                        start_method="spawn")
     got = sorted(q.get() for _ in range(WORLD))
     assert got == [(0, "ok"), (1, "ok")], got
+
+
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("which", ["7b", "70b"])
+def test_plan_tiles_full_shapes_at_4_and_8_ranks(faber, which, world):
+    """The 7B (43 FFN super-blocks: uneven split) and 70B (8 kv heads: one
+    per rank at 8) plans: every rank's blocks are whole super-blocks, tile
+    the rows (column-parallel) or the columns (row-parallel) in rank order,
+    and the FFN split of gate/up matches the input split of down."""
+    import ctypes
+
+    from faber_runtime_b200 import LLAMA2_7B, LLAMA3_70B, _lib
+    cfg = LLAMA2_7B if which == "7b" else LLAMA3_70B
+
+    def shard(rank, name):
+        c = cfg.c_struct(tp_size=world, tp_rank=rank)
+        out = (ctypes.c_uint64 * 6)()
+        _lib.call("faber_gpu_v2_tp_shard", ctypes.byref(c), name.encode(), ctypes.addressof(out))
+        return tuple(int(v) for v in out)
+
+    col = ["attn_q", "attn_k", "attn_v", "ffn_gate", "ffn_up"]
+    for slot in col + ["attn_output", "ffn_down"]:
+        parts = [shard(r, f"blk.3.{slot}.weight") for r in range(world)]
+        rows, cols = parts[0][:2]
+        if slot in col:
+            starts = [p[2] for p in parts]
+            assert starts == sorted(starts) and starts[0] == 0
+            assert all(p[2] + p[3] == q[2] for p, q in zip(parts, parts[1:])), slot
+            assert sum(p[3] for p in parts) == rows and all(p[3] > 0 for p in parts)
+            if slot.startswith("attn"):
+                assert all(p[3] % cfg.head_dim == 0 for p in parts)
+            else:
+                assert all(p[2] % 256 == 0 and p[3] % 256 == 0 for p in parts)
+        else:
+            assert all(p[4] + p[5] == q[4] for p, q in zip(parts, parts[1:])), slot
+            assert sum(p[5] for p in parts) == cols and all(p[4] % 256 == 0 for p in parts)
+    for r in range(world):  # down's input block is this rank's FFN block
+        g, dn = shard(r, "blk.0.ffn_gate.weight"), shard(r, "blk.0.ffn_down.weight")
+        assert (g[2], g[3]) == (dn[4], dn[5])
+        o, q = shard(r, "blk.0.attn_output.weight"), shard(r, "blk.0.attn_q.weight")
+        assert (q[2], q[3]) == (o[4], o[5])
+    heads = [shard(r, "output.weight") for r in range(world)]
+    assert sum(h[3] for h in heads) == cfg.vocab
