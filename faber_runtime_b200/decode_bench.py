@@ -1,8 +1,11 @@
 """Decode-step micro-benchmark: greedy tokens over an installed K/V prefix.
 
     python -m faber_runtime_b200.decode_bench --layers 32 --ctx 2048 --steps 8
+    python -m faber_runtime_b200.decode_bench --model 70b --ctx 4096 --steps 32
 
-Builds the Llama-2-7B-shape model (optionally cut to ``--layers``), installs
+Builds the Llama-2-7B-shape model (or, with ``--model 70b``, the 70B shape:
+80 layers, d 8192, 64/8 heads, FFN 28672, vocab 128256; 39 GB of Q4_K), cut
+to ``--layers`` when given, installs
 a ``--ctx``-position K/V prefix in every layer directly (the same seeded
 random rows in each layer, instead of decoding ``--ctx`` tokens), pushes one
 token, then runs ``--warmup`` and ``--steps`` greedy tokens as CUDA-graph
@@ -19,7 +22,8 @@ import json
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--model", choices=("7b", "70b"), default="7b")
+    ap.add_argument("--layers", type=int, default=0, help="0: every layer of the shape")
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=2)
@@ -27,8 +31,10 @@ def main() -> None:
 
     import torch
 
-    from . import LLAMA2_7B, DeviceModel, ForwardRun, synth
-    cfg = LLAMA2_7B.with_layers(args.layers)
+    from . import LLAMA2_7B, LLAMA3_70B, DeviceModel, ForwardRun, synth
+    cfg = LLAMA2_7B if args.model == "7b" else LLAMA3_70B
+    if args.layers:
+        cfg = cfg.with_layers(args.layers)
     seed = 20261201
     model = DeviceModel(cfg, synth.model_tensors(cfg, seed))
     run = ForwardRun(model, context_length=args.ctx + args.warmup + args.steps + 4)
@@ -44,7 +50,7 @@ def main() -> None:
     ms = run.last_greedy_ms()
     kv_bytes = cfg.n_layers * 2 * span * 2 * (args.ctx + args.warmup + args.steps // 2)
     w_bytes = cfg.linear_bytes() + cfg.head_bytes()
-    print(json.dumps({"layers": cfg.n_layers, "ctx": args.ctx, "steps": args.steps,
+    print(json.dumps({"model": cfg.name, "layers": cfg.n_layers, "ctx": args.ctx, "steps": args.steps,
                       "ms_per_token": ms / args.steps, "tok_s": args.steps / (ms * 1e-3),
                       "weight_bytes": w_bytes, "kv_bytes": kv_bytes,
                       "gbs": (w_bytes + kv_bytes) / (ms / args.steps * 1e-3) / 1e9,

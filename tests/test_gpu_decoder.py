@@ -171,6 +171,34 @@ def test_7b_shape_two_layers_over_prefix(cuda):
     assert len(drun) == n_prefix + 4
 
 
+def test_70b_shape_one_layer_over_prefix(cuda):
+    """The 70B shape at full width (d 8192, 64/8 heads of 128, FFN 28672 =
+    112 super-blocks, vocab 128256) cut to one layer, over an installed
+    96-position K/V prefix: logits of three pushes within tolerance and the
+    same greedy argmax."""
+    import oracle as o
+    from faber_runtime_b200 import LLAMA3_70B, ForwardRun, synth
+    cfg = LLAMA3_70B.with_layers(1)
+    om, dm, _ = build_pair(cfg, 70, norms="random")
+    n_prefix = 96
+    span = cfg.n_kv_heads * cfg.head_dim
+    orun = o.OracleRun(om, n_prefix + 8)
+    drun = ForwardRun(dm, context_length=n_prefix + 8)
+    k = synth.normal(70, 1000, n_prefix * span, 0.0, 4.0)
+    v = synth.normal(70, 2000, n_prefix * span, 0.0, 4.0)
+    orun.set_prefix(0, k, v, n_prefix)
+    drun.set_prefix(0, k, v, n_prefix)
+    for t in synth.tokens(70, 5, 3, 32000):
+        orun.push_token(int(t))
+        drun.push_token(int(t))
+        ref = orun.position_logits()
+        got = drun.position_logits()
+        within(got, ref)
+        assert o.top1_non_eog(got) == o.top1_non_eog(ref)
+    drun.close()
+    dm.close()
+
+
 PREFILL_CASES = [
     # (model, prompt length): the prompt goes through the tensor-core prompt
     # pass (tcgen05 GEMMs, tensor-core flash attention) in chunks of 2048
