@@ -13,8 +13,9 @@
 // One CTA computes a 128 x 256 tile of D = W * Xs^T (128 weight rows x 128
 // tokens as 256 hi/lo columns) over K in steps of 64:
 //   * warp 0, lane 0: TMA loads of the Xs tile (128-byte swizzle, no
-//     multicast) into a 3-stage ring, and bulk copies of the raw Q4_K tile
-//     items (one super-block column at a time) into a double buffer;
+//     multicast) into a 3-stage ring, and the raw Q4_K tile items (one
+//     super-block column at a time, two columns ahead) into a 4-slot ring:
+//     quant rows by a 128-byte-swizzled 4-D TMA, headers by bulk copies;
 //   * warp 1: allocates 256 TMEM columns, and lane 0 issues
 //     tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256, K 16) from the two
 //     shared-memory descriptors, committing each stage back to its mbarrier;
@@ -42,12 +43,20 @@ constexpr int kPgThreads = 320;  // warp 0 loads, warp 1 MMA, warps 2-9 dequant 
 constexpr int kPgDequantWarps = 8;
 constexpr int kPgATile = kPgBM * kPgBK * 2;                         // 16 KB
 constexpr int kPgBTile = kPgBN * kPgBK * 2;                         // 32 KB
-constexpr int kPgRaw = (kPgBM / kTileRows) * kTileItemBytes;        // 18 KB
+constexpr int kPgRaw = (kPgBM / kTileRows) * kTileItemBytes;        // 18 KB per column
+constexpr int kPgRawQuant = kPgBM * 128;                            // quant rows (16 KB, swizzled)
+constexpr int kPgRawHdr = kTileRows * 16;                           // one tile's 16 headers
 constexpr int kPgSmemA = 0;
 constexpr int kPgSmemB = kPgSmemA + kPgStages * kPgATile;           // 48 KB
 constexpr int kPgSmemRaw = kPgSmemB + kPgStages * kPgBTile;         // 144 KB
-constexpr int kPgSmemBars = kPgSmemRaw + 2 * kPgRaw;                // 180 KB
+constexpr int kPgRawBufs = 4;      // raw super-block columns in flight
+constexpr int kPgRawAhead = 2;     // the producer loads column sbk + 2 while the B ring is at sbk
+constexpr int kPgSmemBars = kPgSmemRaw + kPgRawBufs * kPgRaw;       // 216 KB
 constexpr int kPgSmemBytes = kPgSmemBars + 256 + 1024;              // + barriers + alignment slack
+static_assert(kPgSmemBytes <= 227 * 1024, "prefill GEMM shared memory above the per-CTA limit");
+static_assert((3 * kPgStages + 2 * kPgRawBufs + 1) * 8 + 4 <= 256, "barrier area");
+static_assert(kPgRawQuant + (kPgBM / kTileRows) * kPgRawHdr == kPgRaw && kPgRaw % 1024 == 0,
+              "raw slot: 1024-aligned swizzled quant rows, then headers");
 
 // Epilogues of the prefill GEMM (per output element y[t][m]).
 enum PrefillEpi : int {
@@ -80,6 +89,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// 4-D tiled load (the Q4_K quant rows of one super-block column: 128 bytes
+// x 16 rows x 1 column x 8 tiles), no multicast
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
       : "memory");
 }
 
@@ -144,7 +164,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // ---- the kernel -----------------------------------------------------------
 template <int EPI>
 __global__ void __launch_bounds__(kPgThreads, 1)
-    prefill_gemm_kernel(const __grid_constant__ CUtensorMap xs_map, const PrefillGemmArgs a) {
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap xs_map,
+                        const __grid_constant__ CUtensorMap q_map, const PrefillGemmArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -155,13 +176,15 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   uint64_t* b_full = bars;                    // [3] TMA of Xs landed
   uint64_t* a_full = bars + kPgStages;        // [3] 4 dequant warps wrote A
   uint64_t* s_done = bars + 2 * kPgStages;    // [3] MMAs of the stage finished
-  uint64_t* raw_full = bars + 3 * kPgStages;  // [2]
-  uint64_t* raw_empty = raw_full + 2;         // [2]
-  uint64_t* tile_done = raw_empty + 2;        // [1]
+  uint64_t* raw_full = bars + 3 * kPgStages;  // [kPgRawBufs]
+  uint64_t* raw_empty = raw_full + kPgRawBufs;
+  uint64_t* tile_done = raw_empty + kPgRawBufs;  // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x, n_tile = blockIdx.y;
+  // the column tiles of one weight tile are neighbours in launch order, so
+  // its Q4_K bytes come from DRAM once and from L2 for the others
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
   const int nkb = a.nb * (256 / kPgBK);  // K steps
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPgStages; ++s) {
@@ -169,7 +192,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
       mbar_init(&a_full[s], kPgDequantWarps);
       mbar_init(&s_done[s], 1);
     }
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < kPgRawBufs; ++r) {
       mbar_init(&raw_full[r], 1);
       mbar_init(&raw_empty[r], kPgDequantWarps);
     }
@@ -189,21 +212,28 @@ __global__ void __launch_bounds__(kPgThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      uint64_t policy;
-      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      uint64_t policy;  // the 16 column tiles of a weight tile read it close together
+      asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(policy));
       const int tiles_here = min(kPgBM / kTileRows, a.n_tiles - m_tile * (kPgBM / kTileRows));
+      // raw Q4_K items of super-block column sbk into ring slot sbk % kPgRawBufs:
+      // the quant rows by one swizzled 4-D TMA (out-of-range tiles read 0),
+      // the 256-byte header groups by bulk copies
+      auto load_raw = [&](int sbk) {
+        const int r = sbk % kPgRawBufs;
+        uint8_t* slot = sraw + r * kPgRaw;
+        if (sbk >= kPgRawBufs) mbar_wait(&raw_empty[r], ((sbk / kPgRawBufs) - 1) & 1);
+        mbar_arrive_expect_tx(&raw_full[r], (uint32_t)(kPgRawQuant + tiles_here * kPgRawHdr));
+        tma_load_4d(slot, &q_map, 0, 0, sbk, m_tile * (kPgBM / kTileRows), &raw_full[r]);
+        for (int i = 0; i < tiles_here; ++i)
+          bulk_g2s(slot + kPgRawQuant + i * kPgRawHdr,
+                   a.w + ((size_t)(m_tile * (kPgBM / kTileRows) + i) * a.nb + sbk) * kTileItemBytes,
+                   kPgRawHdr, &raw_full[r], policy);
+      };
+      for (int sbk = 0; sbk < min(kPgRawAhead, a.nb); ++sbk) load_raw(sbk);
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % kPgStages;
         if (kb >= kPgStages) mbar_wait(&s_done[s], ((kb / kPgStages) - 1) & 1);
-        if (kb % 4 == 0) {  // raw Q4_K items of super-block column kb / 4
-          const int sbk = kb / 4, r = sbk & 1;
-          if (sbk >= 2) mbar_wait(&raw_empty[r], ((sbk / 2) - 1) & 1);
-          mbar_arrive_expect_tx(&raw_full[r], (uint32_t)(tiles_here * kTileItemBytes));
-          for (int i = 0; i < tiles_here; ++i)
-            bulk_g2s(sraw + r * kPgRaw + i * kTileItemBytes,
-                     a.w + ((size_t)(m_tile * (kPgBM / kTileRows) + i) * a.nb + sbk) * kTileItemBytes,
-                     kTileItemBytes, &raw_full[r], policy);
-        }
+        if (kb % 4 == 0 && kb / 4 + kPgRawAhead < a.nb) load_raw(kb / 4 + kPgRawAhead);
         mbar_arrive_expect_tx(&b_full[s], (uint32_t)kPgBTile);
         tma_load_2d(sb + s * kPgBTile, &xs_map, kb * kPgBK, n_tile * kPgBN, &b_full[s]);
       }
@@ -237,14 +267,17 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     asm("mov.b32 %0, 0x64006400;" : "=r"(lc.m1024));
     asm("mov.b32 %0, 0x54005400;" : "=r"(lc.m64));
     for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kPgStages, sbk = kb / 4, r = sbk & 1, chunk = kb % 4;
-      if (chunk == 0) mbar_wait(&raw_full[r], (sbk / 2) & 1);
+      const int s = kb % kPgStages, sbk = kb / 4, r = sbk % kPgRawBufs, chunk = kb % 4;
+      if (chunk == 0) mbar_wait(&raw_full[r], (sbk / kPgRawBufs) & 1);
       if (kb >= kPgStages) mbar_wait(&s_done[s], ((kb / kPgStages) - 1) & 1);
-      const uint8_t* item = sraw + r * kPgRaw + q_in_tile * kTileItemBytes;
-      const uint4 hdr = *reinterpret_cast<const uint4*>(item + 16 * row16);
-      const uint8_t* qs = item + 256 + 128 * row16 + 32 * chunk;
-      const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
+      const uint8_t* slot = sraw + r * kPgRaw;
+      const uint4 hdr =
+          *reinterpret_cast<const uint4*>(slot + kPgRawQuant + q_in_tile * kPgRawHdr + 16 * row16);
+      // quant row `row`: 16-byte chunk c sits at chunk c ^ (row & 7) (the TMA's
+      // 128-byte swizzle), so 8 consecutive rows hit 8 distinct bank groups
+      const uint8_t* qrow = slot + row * 128;
+      const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + (((2 * chunk) ^ (row & 7)) << 4));
+      const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + (((2 * chunk + 1) ^ (row & 7)) << 4));
       {
         const uint32_t k = 2u * (uint32_t)(chunk & 1);
         lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
@@ -453,9 +486,10 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
-// D += A(16x16 f16, row) * B(16x8 f16, col), f32 accumulate
+// D += A(16x16 f16, row) * B(16x8 f16, col), f32 accumulate (registers
+// only, so the compiler may interleave independent accumulators)
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -582,14 +616,21 @@ __global__ void __launch_bounds__(kFaThreads) prefill_flash_kernel(const float* 
       const uint32_t qo = fa_off<HD>(warp * 16 + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1));
       ldsm_x4(qh_base + qo, ah);
       ldsm_x4(ql_base + qo, al);
+      uint32_t b[4][4];
+#pragma unroll
+      for (int np = 0; np < 4; ++np)
+        ldsm_x4(kbase + fa_off<HD>(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b[np]);
+      // the hi products of all 8 tiles, then the lo ones: no back-to-back
+      // MMAs on one accumulator
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
-        uint32_t b[4];
-        ldsm_x4(kbase + fa_off<HD>(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
-        mma16816(sacc[2 * np], ah, b[0], b[1]);
-        mma16816(sacc[2 * np], al, b[0], b[1]);
-        mma16816(sacc[2 * np + 1], ah, b[2], b[3]);
-        mma16816(sacc[2 * np + 1], al, b[2], b[3]);
+        mma16816(sacc[2 * np], ah, b[np][0], b[np][1]);
+        mma16816(sacc[2 * np + 1], ah, b[np][2], b[np][3]);
+      }
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        mma16816(sacc[2 * np], al, b[np][0], b[np][1]);
+        mma16816(sacc[2 * np + 1], al, b[np][2], b[np][3]);
       }
     }
     // scale, mask, online softmax (rows r = lane/4 and r + 8; 4 lanes per row)
@@ -653,8 +694,8 @@ __global__ void __launch_bounds__(kFaThreads) prefill_flash_kernel(const float* 
         uint32_t b[4];
         ldsm_x4_t(vbase + fa_off<HD>(16 * j + (mi & 1) * 8 + r8, 2 * dp + (mi >> 1)), b);
         mma16816(o_acc[2 * dp], ph, b[0], b[1]);
-        mma16816(o_acc[2 * dp], pl, b[0], b[1]);
         mma16816(o_acc[2 * dp + 1], ph, b[2], b[3]);
+        mma16816(o_acc[2 * dp], pl, b[0], b[1]);
         mma16816(o_acc[2 * dp + 1], pl, b[2], b[3]);
       }
     }
