@@ -900,23 +900,8 @@ void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGe
   a.nb = W.nb;
   a.m_rows = W.rows;
   a.n_tok = n_tok;
-  // quant bytes of the tile items as [tile][column][16 rows][128 B]
-  CUtensorMap qmap;
-  {
-    const cuuint64_t dims[4] = {128, kTileRows, (cuuint64_t)W.nb, (cuuint64_t)W.n_tiles};
-    const cuuint64_t strides[3] = {128, kTileItemBytes, (cuuint64_t)W.nb * kTileItemBytes};
-    const cuuint32_t box[4] = {128, kTileRows, 1, kPgBM / kTileRows};
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    const CUresult r = tmap_encoder()(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
-                                      const_cast<uint8_t*>(W.w.as<uint8_t>()) + kTileRows * 16, dims,
-                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    require(r == CUDA_SUCCESS, FABER_STATUS_CUDA_ERROR,
-            "cuTensorMapEncodeTiled (weights) failed (" + std::to_string((int)r) + ")");
-  }
   const dim3 grid((2 * n_tok + kPgBN - 1) / kPgBN, (W.rows + kPgBM - 1) / kPgBM);
-  prefill_gemm_kernel<EPI><<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, qmap, a);
+  prefill_gemm_kernel<EPI><<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, a);
   FABER_CUDA(cudaGetLastError());
 }
 

@@ -13,17 +13,17 @@
 // One CTA computes a 128 x 256 tile of D = W * Xs^T (128 weight rows x 128
 // tokens as 256 hi/lo columns) over K in steps of 64:
 //   * warp 0, lane 0: TMA loads of the Xs tile (128-byte swizzle, no
-//     multicast) into a 3-stage ring, and the raw Q4_K tile items (one
-//     super-block column at a time, two columns ahead) into a 4-slot ring:
-//     quant rows by a 128-byte-swizzled 4-D TMA, headers by bulk copies;
+//     multicast) into a 4-stage ring;
 //   * warp 1: allocates 256 TMEM columns, and lane 0 issues
 //     tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256, K 16) from the two
 //     shared-memory descriptors, committing each stage back to its mbarrier;
-//   * warps 2-9 (two per TMEM lane quadrant): dequantize 128 rows x 64
-//     weights per stage (a thread makes one row's low- or high-nibble half)
-//     with the GEMV's exact f16 formation, write them in the 128-byte-swizzled
-//     K-major layout the A descriptor reads, and finally read the
-//     accumulators (tcgen05.ld) for the epilogue.
+//   * warps 2-9 (two per TMEM lane quadrant): fetch their rows' Q4_K bytes
+//     from global memory into registers one super-block column ahead,
+//     dequantize 128 rows x 64 weights per stage (a thread makes one row's
+//     low- or high-nibble half) with the GEMV's exact f16 formation, write
+//     them in the 128-byte-swizzled K-major layout the A descriptor reads
+//     (a 6-stage ring; a slot is awaited only just before its store), and
+//     finally read the accumulators (tcgen05.ld) for the epilogue.
 // Every wait is bounded (g_pipe_error = 1 on expiry, then the CTA proceeds;
 // barriers stay balanced).
 #pragma once
@@ -38,25 +38,20 @@ namespace faber {
 constexpr int kPgBM = 128;
 constexpr int kPgBN = 256;
 constexpr int kPgBK = 64;
-constexpr int kPgStages = 3;
+constexpr int kPgAStages = 6;    // dequantized weight tiles in flight
+constexpr int kPgBStages = 4;    // activation tiles in flight
 constexpr int kPgThreads = 320;  // warp 0 loads, warp 1 MMA, warps 2-9 dequant + epilogue
 constexpr int kPgDequantWarps = 8;
 constexpr int kPgATile = kPgBM * kPgBK * 2;                         // 16 KB
 constexpr int kPgBTile = kPgBN * kPgBK * 2;                         // 32 KB
-constexpr int kPgRaw = (kPgBM / kTileRows) * kTileItemBytes;        // 18 KB per column
-constexpr int kPgRawQuant = kPgBM * 128;                            // quant rows (16 KB, swizzled)
-constexpr int kPgRawHdr = kTileRows * 16;                           // one tile's 16 headers
 constexpr int kPgSmemA = 0;
-constexpr int kPgSmemB = kPgSmemA + kPgStages * kPgATile;           // 48 KB
-constexpr int kPgSmemRaw = kPgSmemB + kPgStages * kPgBTile;         // 144 KB
-constexpr int kPgRawBufs = 4;      // raw super-block columns in flight
-constexpr int kPgRawAhead = 2;     // the producer loads column sbk + 2 while the B ring is at sbk
-constexpr int kPgSmemBars = kPgSmemRaw + kPgRawBufs * kPgRaw;       // 216 KB
-constexpr int kPgSmemBytes = kPgSmemBars + 256 + 1024;              // + barriers + alignment slack
+constexpr int kPgSmemB = kPgSmemA + kPgAStages * kPgATile;          // 96 KB
+constexpr int kPgSmemBars = kPgSmemB + kPgBStages * kPgBTile;       // 224 KB
+constexpr int kPgSmemXs = kPgSmemBars + 256;                         // 128 token row scales
+constexpr int kPgSmemBytes = kPgSmemXs + (kPgBN / 2) * 4 + 1024;     // + alignment slack
 static_assert(kPgSmemBytes <= 227 * 1024, "prefill GEMM shared memory above the per-CTA limit");
-static_assert((3 * kPgStages + 2 * kPgRawBufs + 1) * 8 + 4 <= 256, "barrier area");
-static_assert(kPgRawQuant + (kPgBM / kTileRows) * kPgRawHdr == kPgRaw && kPgRaw % 1024 == 0,
-              "raw slot: 1024-aligned swizzled quant rows, then headers");
+static_assert((2 * kPgAStages + 2 * kPgBStages + 1) * 8 + 4 <= 256, "barrier area");
+static_assert(kPgSmemB % 1024 == 0, "128-byte-swizzled tiles start on 1024-byte boundaries");
 
 // Epilogues of the prefill GEMM (per output element y[t][m]).
 enum PrefillEpi : int {
@@ -89,17 +84,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// 4-D tiled load (the Q4_K quant rows of one super-block column: 128 bytes
-// x 16 rows x 1 column x 8 tiles), no multicast
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            int c3, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
       : "memory");
 }
 
@@ -164,37 +148,38 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // ---- the kernel -----------------------------------------------------------
 template <int EPI>
 __global__ void __launch_bounds__(kPgThreads, 1)
-    prefill_gemm_kernel(const __grid_constant__ CUtensorMap xs_map,
-                        const __grid_constant__ CUtensorMap q_map, const PrefillGemmArgs a) {
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap xs_map, const PrefillGemmArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* sa = smem + kPgSmemA;
   uint8_t* sb = smem + kPgSmemB;
-  uint8_t* sraw = smem + kPgSmemRaw;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPgSmemBars);
-  uint64_t* b_full = bars;                    // [3] TMA of Xs landed
-  uint64_t* a_full = bars + kPgStages;        // [3] 4 dequant warps wrote A
-  uint64_t* s_done = bars + 2 * kPgStages;    // [3] MMAs of the stage finished
-  uint64_t* raw_full = bars + 3 * kPgStages;  // [kPgRawBufs]
-  uint64_t* raw_empty = raw_full + kPgRawBufs;
-  uint64_t* tile_done = raw_empty + kPgRawBufs;  // [1]
+  uint64_t* b_full = bars;                     // [kPgBStages] TMA of Xs landed
+  uint64_t* b_empty = b_full + kPgBStages;     // [kPgBStages] MMAs reading it finished
+  uint64_t* a_full = b_empty + kPgBStages;     // [kPgAStages] the dequant warps wrote A
+  uint64_t* a_empty = a_full + kPgAStages;     // [kPgAStages] MMAs reading it finished
+  uint64_t* tile_done = a_empty + kPgAStages;  // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_done + 1);
+  float* xs_s = reinterpret_cast<float*>(smem + kPgSmemXs);  // row scales of this tile's tokens
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the column tiles of one weight tile are neighbours in launch order, so
   // its Q4_K bytes come from DRAM once and from L2 for the others
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
   const int nkb = a.nb * (256 / kPgBK);  // K steps
+  if (threadIdx.x < kPgBN / 2) {
+    const int t = n_tile * (kPgBN / 2) + threadIdx.x;
+    xs_s[threadIdx.x] = t < a.n_tok ? a.xscale[t] : 0.0f;
+  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPgStages; ++s) {
+    for (int s = 0; s < kPgBStages; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&a_full[s], kPgDequantWarps);
-      mbar_init(&s_done[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
-    for (int r = 0; r < kPgRawBufs; ++r) {
-      mbar_init(&raw_full[r], 1);
-      mbar_init(&raw_empty[r], kPgDequantWarps);
+    for (int s = 0; s < kPgAStages; ++s) {
+      mbar_init(&a_full[s], kPgDequantWarps);
+      mbar_init(&a_empty[s], 1);
     }
     mbar_init(tile_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -212,28 +197,9 @@ __global__ void __launch_bounds__(kPgThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      uint64_t policy;  // the 16 column tiles of a weight tile read it close together
-      asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(policy));
-      const int tiles_here = min(kPgBM / kTileRows, a.n_tiles - m_tile * (kPgBM / kTileRows));
-      // raw Q4_K items of super-block column sbk into ring slot sbk % kPgRawBufs:
-      // the quant rows by one swizzled 4-D TMA (out-of-range tiles read 0),
-      // the 256-byte header groups by bulk copies
-      auto load_raw = [&](int sbk) {
-        const int r = sbk % kPgRawBufs;
-        uint8_t* slot = sraw + r * kPgRaw;
-        if (sbk >= kPgRawBufs) mbar_wait(&raw_empty[r], ((sbk / kPgRawBufs) - 1) & 1);
-        mbar_arrive_expect_tx(&raw_full[r], (uint32_t)(kPgRawQuant + tiles_here * kPgRawHdr));
-        tma_load_4d(slot, &q_map, 0, 0, sbk, m_tile * (kPgBM / kTileRows), &raw_full[r]);
-        for (int i = 0; i < tiles_here; ++i)
-          bulk_g2s(slot + kPgRawQuant + i * kPgRawHdr,
-                   a.w + ((size_t)(m_tile * (kPgBM / kTileRows) + i) * a.nb + sbk) * kTileItemBytes,
-                   kPgRawHdr, &raw_full[r], policy);
-      };
-      for (int sbk = 0; sbk < min(kPgRawAhead, a.nb); ++sbk) load_raw(sbk);
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kPgStages;
-        if (kb >= kPgStages) mbar_wait(&s_done[s], ((kb / kPgStages) - 1) & 1);
-        if (kb % 4 == 0 && kb / 4 + kPgRawAhead < a.nb) load_raw(kb / 4 + kPgRawAhead);
+        const int s = kb % kPgBStages;
+        if (kb >= kPgBStages) mbar_wait(&b_empty[s], ((kb / kPgBStages) - 1) & 1);
         mbar_arrive_expect_tx(&b_full[s], (uint32_t)kPgBTile);
         tma_load_2d(sb + s * kPgBTile, &xs_map, kb * kPgBK, n_tile * kPgBN, &b_full[s]);
       }
@@ -242,79 +208,90 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(kPgBM, kPgBN);
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kPgStages;
-        const uint32_t ph = (kb / kPgStages) & 1;
-        mbar_wait(&a_full[s], ph);
-        mbar_wait(&b_full[s], ph);
+        const int sa_i = kb % kPgAStages, sb_i = kb % kPgBStages;
+        mbar_wait(&a_full[sa_i], (kb / kPgAStages) & 1);
+        mbar_wait(&b_full[sb_i], (kb / kPgBStages) & 1);
         tc_fence_after();
-        const uint32_t a0 = smem_addr(sa + s * kPgATile), b0 = smem_addr(sb + s * kPgBTile);
+        const uint32_t a0 = smem_addr(sa + sa_i * kPgATile), b0 = smem_addr(sb + sb_i * kPgBTile);
 #pragma unroll
         for (int j = 0; j < kPgBK / 16; ++j)  // K 16 = 32 bytes along the swizzled row
           umma_f16(tmem, umma_desc_sw128(a0 + 32 * j), umma_desc_sw128(b0 + 32 * j), idesc,
                    (kb | j) != 0);
-        umma_commit(&s_done[s]);
+        umma_commit(&a_empty[sa_i]);
+        umma_commit(&b_empty[sb_i]);
       }
       umma_commit(tile_done);
     }
   } else {
     // dequant: thread i of warps 2-9 owns weight row i % 128 of the tile, the
     // low-nibble half (k 0..31 of the step, warps 2-5) or the high-nibble half
-    // (k 32..63, warps 6-9): two dequantizing warps per scheduler
+    // (k 32..63, warps 6-9): two dequantizing warps per scheduler. Each
+    // thread reads its row's 16-byte header and 128 quant bytes of a
+    // super-block column straight from global memory (L2: the 16 column tiles
+    // of this weight tile read the same bytes), one column ahead.
     const int i = threadIdx.x - 64;
     const int row = i & (kPgBM - 1), half = i >> 7;
     const int q_in_tile = row >> 4, row16 = row & 15;
+    const int tile = m_tile * (kPgBM / kTileRows) + q_in_tile;
+    const bool row_live = tile < a.n_tiles;  // rows past the weight read as zero blocks
+    const uint8_t* wrow = a.w + (size_t)(row_live ? tile : 0) * a.nb * kTileItemBytes;
     LaneConst lc;
     asm("mov.b32 %0, 0x64006400;" : "=r"(lc.m1024));
     asm("mov.b32 %0, 0x54005400;" : "=r"(lc.m64));
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kPgStages, sbk = kb / 4, r = sbk % kPgRawBufs, chunk = kb % 4;
-      if (chunk == 0) mbar_wait(&raw_full[r], (sbk / kPgRawBufs) & 1);
-      if (kb >= kPgStages) mbar_wait(&s_done[s], ((kb / kPgStages) - 1) & 1);
-      const uint8_t* slot = sraw + r * kPgRaw;
-      const uint4 hdr =
-          *reinterpret_cast<const uint4*>(slot + kPgRawQuant + q_in_tile * kPgRawHdr + 16 * row16);
-      // quant row `row`: 16-byte chunk c sits at chunk c ^ (row & 7) (the TMA's
-      // 128-byte swizzle), so 8 consecutive rows hit 8 distinct bank groups
-      const uint8_t* qrow = slot + row * 128;
-      const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + (((2 * chunk) ^ (row & 7)) << 4));
-      const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + (((2 * chunk + 1) ^ (row & 7)) << 4));
-      {
-        const uint32_t k = 2u * (uint32_t)(chunk & 1);
-        lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
-      }
-      const RowScales3 sc = row_scales3(hdr, chunk, lc);
-      // this half's scale constants: sub-block 2c (low nibbles) or 2c + 1
-      const uint32_t sc2 = half ? sc.schi2 : sc.sclo2, c2 = half ? sc.chi2 : sc.clo2;
-      const float nm = half ? sc.nm2 : sc.nm1;
-      uint32_t h[16];  // 32 f16: k 32 * half + 0..31
+    uint4 nh, nq[8];
+    auto fetch = [&](int sbk) {
+      const uint8_t* item = wrow + (size_t)sbk * kTileItemBytes;
+      const uint4* qp = reinterpret_cast<const uint4*>(item + kTileRows * 16 + 128 * row16);
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      nh = row_live ? __ldg(reinterpret_cast<const uint4*>(item + 16 * row16)) : z;
 #pragma unroll
-      for (int wd = 0; wd < 8; ++wd) {
-        const uint32_t w = word_of(wd < 4 ? q0 : q1, wd & 3);
-        const uint32_t u = w >> 8;
-        // (k0, k2) from bytes 0/2 and (k1, k3) from bytes 1/3 of the word
-        const uint32_t p02 = half ? hfma2_u(and_or<0x00f000f0u>(w, lc.m64), sc2, c2)
-                                  : hfma2_u(and_or<0x000f000fu>(w, lc.m1024), sc2, c2);
-        const uint32_t p13 = half ? hfma2_u(and_or<0x00f000f0u>(u, lc.m64), sc2, c2)
-                                  : hfma2_u(and_or<0x000f000fu>(u, lc.m1024), sc2, c2);
-        const float2 a02 = mixed_fma_pair(p02, sc.dword, nm);
-        const float2 a13 = mixed_fma_pair(p13, sc.dword, nm);
-        const uint32_t v02 = pack_half2(a02.x, a02.y), v13 = pack_half2(a13.x, a13.y);
-        h[2 * wd] = prmt<0x5410>(v02, v13);      // (k0, k1)
-        h[2 * wd + 1] = prmt<0x7632>(v02, v13);  // (k2, k3)
-      }
-      {
+      for (int j = 0; j < 8; ++j) nq[j] = row_live ? __ldg(qp + j) : z;
+    };
+    fetch(0);
+    for (int sbk = 0; sbk < a.nb; ++sbk) {
+      const uint4 hdr = nh;
+      uint4 q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = nq[j];
+      if (sbk + 1 < a.nb) fetch(sbk + 1);
+#pragma unroll
+      for (int chunk = 0; chunk < 4; ++chunk) {
+        const int kb = sbk * 4 + chunk, s = kb % kPgAStages;
+        {
+          const uint32_t k = 2u * (uint32_t)(chunk & 1);
+          lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
+        }
+        const RowScales3 sc = row_scales3(hdr, chunk, lc);
+        // this half's scale constants: sub-block 2c (low nibbles) or 2c + 1
+        const uint32_t sc2 = half ? sc.schi2 : sc.sclo2, c2 = half ? sc.chi2 : sc.clo2;
+        const float nm = half ? sc.nm2 : sc.nm1;
+        uint32_t h[16];  // 32 f16: k 32 * half + 0..31
+#pragma unroll
+        for (int wd = 0; wd < 8; ++wd) {
+          const uint32_t w = word_of(q[2 * chunk + (wd >> 2)], wd & 3);
+          const uint32_t u = w >> 8;
+          // (k0, k2) from bytes 0/2 and (k1, k3) from bytes 1/3 of the word
+          const uint32_t p02 = half ? hfma2_u(and_or<0x00f000f0u>(w, lc.m64), sc2, c2)
+                                    : hfma2_u(and_or<0x000f000fu>(w, lc.m1024), sc2, c2);
+          const uint32_t p13 = half ? hfma2_u(and_or<0x00f000f0u>(u, lc.m64), sc2, c2)
+                                    : hfma2_u(and_or<0x000f000fu>(u, lc.m1024), sc2, c2);
+          const float2 a02 = mixed_fma_pair(p02, sc.dword, nm);
+          const float2 a13 = mixed_fma_pair(p13, sc.dword, nm);
+          const uint32_t v02 = pack_half2(a02.x, a02.y), v13 = pack_half2(a13.x, a13.y);
+          h[2 * wd] = prmt<0x5410>(v02, v13);      // (k0, k1)
+          h[2 * wd + 1] = prmt<0x7632>(v02, v13);  // (k2, k3)
+        }
+        // the slot is free once the MMAs of step kb - kPgAStages finished
+        if (kb >= kPgAStages) mbar_wait(&a_empty[s], ((kb / kPgAStages) - 1) & 1);
         uint8_t* arow = sa + s * kPgATile + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc)
           *reinterpret_cast<uint4*>(arow + (((4 * half + cc) ^ (row & 7)) << 4)) =
               make_uint4(h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
-      }
-      // generic-proxy writes become visible to the tensor core's async proxy
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[s]);
-        if (chunk == 3) mbar_arrive(&raw_empty[r]);
+        // generic-proxy writes become visible to the tensor core's async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s]);
       }
     }
     // epilogue: this warp's TMEM lane quadrant = rows 32 * (warp % 4) ..,
@@ -324,41 +301,68 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     const int quad = warp & 3;
     const int m = m_tile * kPgBM + quad * 32 + lane;
     const int cbeg = half * (kPgBN / 2);
+    const bool row_ok = m < a.m_rows;
     for (int c0 = cbeg; c0 < cbeg + kPgBN / 2; c0 += 32) {
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+      const int tb = (n_tile * kPgBN + c0) / 2;  // first token of these 16 column pairs
+      float y[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = (n_tile * kPgBN + c0) / 2 + j;
-        const bool live = t < a.n_tok;
-        const float y = live ? (v[2 * j] + v[2 * j + 1]) * a.xscale[t] : 0.0f;
-        if (EPI == PG_STORE) {
-          if (live && m < a.m_rows) a.out[(size_t)t * a.ld_out + m] = y;
-        } else if (EPI == PG_RESID) {
-          if (live && m < a.m_rows) a.out[(size_t)t * a.ld_out + m] += y;
-        } else if (EPI == PG_SWIGLU) {
-          // rows 2f (gate) and 2f+1 (up) sit in adjacent lanes
-          const float u = __shfl_xor_sync(0xffffffffu, y, 1);
-          if (live && (lane & 1) == 0 && m + 1 < a.m_rows) {
-            const float sg = __fdiv_rn(y, __fadd_rn(1.0f, expf(-y)));
+      for (int j = 0; j < 16; ++j) y[j] = (v[2 * j] + v[2 * j + 1]) * xs_s[c0 / 2 + j];
+      // every load of a chunk is issued before its stores
+      if (EPI == PG_STORE) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (tb + j < a.n_tok && row_ok) a.out[(size_t)(tb + j) * a.ld_out + m] = y[j];
+      } else if (EPI == PG_RESID) {
+        float old[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          old[j] = (tb + j < a.n_tok && row_ok) ? a.out[(size_t)(tb + j) * a.ld_out + m] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (tb + j < a.n_tok && row_ok) a.out[(size_t)(tb + j) * a.ld_out + m] = old[j] + y[j];
+      } else if (EPI == PG_SWIGLU) {
+        // rows 2f (gate) and 2f+1 (up) sit in adjacent lanes; of each token
+        // pair the even lane finishes the first token and the odd lane the
+        // second, each taking the partner row's value by one shuffle
+        const bool odd = (lane & 1) != 0;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const float mine = odd ? y[2 * jj + 1] : y[2 * jj];
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? y[2 * jj] : y[2 * jj + 1], 1);
+          const float g = odd ? other : mine, u = odd ? mine : other;
+          const int t = tb + 2 * jj + (odd ? 1 : 0);
+          if (t < a.n_tok && (m | 1) < a.m_rows) {
+            const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
             a.out[(size_t)t * a.ld_out + (m >> 1)] = __fmul_rn(sg, u);
           }
-        } else {  // PG_QKV
-          const float y1 = __shfl_xor_sync(0xffffffffu, y, 1);
-          if (live && m < a.m_rows) {
+        }
+      } else {  // PG_QKV
+        const bool rope = m < a.nq + a.nk;  // Q and K rows (warp-uniform: head-aligned)
+        const int kk = (m % a.head_dim) >> 1;
+        float2 cs[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          cs[j] = (rope && tb + j < a.n_tok)
+                      ? a.rope[(size_t)(a.pos0 + tb + j) * (a.head_dim >> 1) + kk]
+                      : make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float y1 = __shfl_xor_sync(0xffffffffu, y[j], 1);
+          const int t = tb + j;
+          if (t < a.n_tok && row_ok) {
             const int pos = a.pos0 + t;
-            if (m < a.nq + a.nk) {
+            if (rope) {
               // rope_norm pair (m even: first, odd: second) with host cos/sin
-              const int kk = (m % a.head_dim) >> 1;
-              const float2 cs = a.rope[(size_t)pos * (a.head_dim >> 1) + kk];
               const bool first = (m & 1) == 0;
-              const float x0 = first ? y : y1, x1 = first ? y1 : y;
-              const float o = first ? __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y))
-                                    : __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+              const float x0 = first ? y[j] : y1, x1 = first ? y1 : y[j];
+              const float o = first ? __fsub_rn(__fmul_rn(x0, cs[j].x), __fmul_rn(x1, cs[j].y))
+                                    : __fadd_rn(__fmul_rn(x0, cs[j].y), __fmul_rn(x1, cs[j].x));
               if (m < a.nq) a.q_out[(size_t)t * a.nq + m] = o;
               else a.k_cache[(size_t)pos * a.nk + (m - a.nq)] = __float2half_rn(o);
             } else {
-              a.v_cache[(size_t)pos * a.nk + (m - a.nq - a.nk)] = __float2half_rn(y);
+              a.v_cache[(size_t)pos * a.nk + (m - a.nq - a.nk)] = __float2half_rn(y[j]);
             }
           }
         }
