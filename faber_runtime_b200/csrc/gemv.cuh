@@ -314,20 +314,35 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
                    (PRO != PRO_NORM_RES || aligned16(a.x2));
   double ss = 0.0;
   float mx = 0.0f;
+  // kXB float4 per thread per batch, every load of a batch issued before any
+  // use (one L2 round trip per batch); each thread still sums its elements
+  // in increasing index order
+  constexpr int kXB = 8;
+  const int n4 = n / 4;
   if (vec) {
-#pragma unroll 4
-    for (int i4 = tid; i4 < n / 4; i4 += NT) {
-      const float4 v = load_x4<PRO>(a, i4);
-      if (PRO != PRO_PLAIN) {
-        const float4 w = reinterpret_cast<const float4*>(a.norm_w)[i4];
-        ss += (double)v.x * (double)v.x;
-        ss += (double)v.y * (double)v.y;
-        ss += (double)v.z * (double)v.z;
-        ss += (double)v.w * (double)v.w;
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * w.x), fabsf(v.y * w.y)),
-                             fmaxf(fabsf(v.z * w.z), fabsf(v.w * w.w))));
-      } else {
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    for (int base = 0; base < n4; base += NT * kXB) {
+      float4 v[kXB], w[kXB];
+#pragma unroll
+      for (int k = 0; k < kXB; ++k) {
+        const int i4 = base + tid + k * NT;
+        if (i4 < n4) {
+          v[k] = load_x4<PRO>(a, i4);
+          if (PRO != PRO_PLAIN) w[k] = reinterpret_cast<const float4*>(a.norm_w)[i4];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kXB; ++k) {
+        if (base + tid + k * NT >= n4) break;
+        if (PRO != PRO_PLAIN) {
+          ss += (double)v[k].x * (double)v[k].x;
+          ss += (double)v[k].y * (double)v[k].y;
+          ss += (double)v[k].z * (double)v[k].z;
+          ss += (double)v[k].w * (double)v[k].w;
+          mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[k].x * w[k].x), fabsf(v[k].y * w[k].y)),
+                               fmaxf(fabsf(v[k].z * w[k].z), fabsf(v[k].w * w[k].w))));
+        } else {
+          mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+        }
       }
     }
   } else {
@@ -364,21 +379,31 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
     xl[xs_index(p)] = __float2half(0.0f);
   }
   if (vec) {
-#pragma unroll 4
-    for (int i4 = tid; i4 < n / 4; i4 += NT) {
-      const float4 v = load_x4<PRO>(a, i4);
-      float4 y = v;
-      if (PRO != PRO_PLAIN) {
-        const float4 w = reinterpret_cast<const float4*>(a.norm_w)[i4];
-        y = make_float4(norm1<PRO>(v.x, scale, w.x), norm1<PRO>(v.y, scale, w.y),
-                        norm1<PRO>(v.z, scale, w.z), norm1<PRO>(v.w, scale, w.w));
+    for (int base = 0; base < n4; base += NT * kXB) {
+      float4 v[kXB], w[kXB];
+#pragma unroll
+      for (int k = 0; k < kXB; ++k) {
+        const int i4 = base + tid + k * NT;
+        if (i4 < n4) {
+          v[k] = load_x4<PRO>(a, i4);
+          if (PRO != PRO_PLAIN) w[k] = reinterpret_cast<const float4*>(a.norm_w)[i4];
+        }
       }
-      if (cta0) {
-        if (PRO == PRO_NORM_RES) reinterpret_cast<float4*>(a.x_sum_out)[i4] = v;
-        if (PRO != PRO_PLAIN && a.x_norm_out) reinterpret_cast<float4*>(a.x_norm_out)[i4] = y;
+#pragma unroll
+      for (int k = 0; k < kXB; ++k) {
+        const int i4 = base + tid + k * NT;
+        if (i4 >= n4) break;
+        float4 y = v[k];
+        if (PRO != PRO_PLAIN)
+          y = make_float4(norm1<PRO>(v[k].x, scale, w[k].x), norm1<PRO>(v[k].y, scale, w[k].y),
+                          norm1<PRO>(v[k].z, scale, w[k].z), norm1<PRO>(v[k].w, scale, w[k].w));
+        if (cta0) {
+          if (PRO == PRO_NORM_RES) reinterpret_cast<float4*>(a.x_sum_out)[i4] = v[k];
+          if (PRO != PRO_PLAIN && a.x_norm_out) reinterpret_cast<float4*>(a.x_norm_out)[i4] = y;
+        }
+        if (PERM) split_store(y.x, y.z, y.y, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
+        else split_store(y.x, y.y, y.z, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
       }
-      if (PERM) split_store(y.x, y.z, y.y, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
-      else split_store(y.x, y.y, y.z, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
     }
   } else {
     for (int i = tid; i < n; i += NT) {
