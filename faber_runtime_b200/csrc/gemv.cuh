@@ -317,11 +317,14 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
   // kXB float4 per thread per batch, every load of a batch issued before any
   // use (one L2 round trip per batch); each thread still sums its elements
   // in increasing index order
-  constexpr int kXB = 8;
+  // (norm weights double the registers of a batch); when one batch covers
+  // the row the values stay in registers for the second pass
+  constexpr int kXB = PRO == PRO_PLAIN ? 12 : 8;
   const int n4 = n / 4;
+  const bool one_batch = n4 <= NT * kXB;
+  float4 v[kXB], w[kXB];
   if (vec) {
     for (int base = 0; base < n4; base += NT * kXB) {
-      float4 v[kXB], w[kXB];
 #pragma unroll
       for (int k = 0; k < kXB; ++k) {
         const int i4 = base + tid + k * NT;
@@ -380,13 +383,14 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
   }
   if (vec) {
     for (int base = 0; base < n4; base += NT * kXB) {
-      float4 v[kXB], w[kXB];
+      if (!one_batch) {
 #pragma unroll
-      for (int k = 0; k < kXB; ++k) {
-        const int i4 = base + tid + k * NT;
-        if (i4 < n4) {
-          v[k] = load_x4<PRO>(a, i4);
-          if (PRO != PRO_PLAIN) w[k] = reinterpret_cast<const float4*>(a.norm_w)[i4];
+        for (int k = 0; k < kXB; ++k) {
+          const int i4 = base + tid + k * NT;
+          if (i4 < n4) {
+            v[k] = load_x4<PRO>(a, i4);
+            if (PRO != PRO_PLAIN) w[k] = reinterpret_cast<const float4*>(a.norm_w)[i4];
+          }
         }
       }
 #pragma unroll
