@@ -245,6 +245,8 @@ inline void validate_config(const FaberModelConfigV1& c) {
   require(c.d_model % 256 == 0, FABER_STATUS_UNSUPPORTED, "d_model must be a multiple of 256");
   require(c.ffn % 32 == 0, FABER_STATUS_UNSUPPORTED, "ffn must be a multiple of 32");
   FABER_ARG(c.tp_size >= 1 && c.tp_rank < c.tp_size, "bad tensor-parallel rank");
+  require(c.tp_size <= (uint32_t)kMaxTp, FABER_STATUS_UNSUPPORTED,
+          "at most " + std::to_string(kMaxTp) + " tensor-parallel ranks");
   if (c.tp_size > 1) {
     require(c.n_heads % c.tp_size == 0 && c.n_kv_heads % c.tp_size == 0, FABER_STATUS_UNSUPPORTED,
             "heads must divide evenly across tensor-parallel ranks");
