@@ -11,11 +11,11 @@ call goes through libfaber_gpu.so. There is no CPU fallback.
 from . import _lib
 from ._lib import FaberError
 from .config import LLAMA2_7B, LLAMA3_70B, TINY, KV_F16, KV_F32, KvCacheLayout, ModelConfig
-from .decoder import DeviceModel, ForwardRun, GreedyRunRecord, OracleError, run_greedy
+from .decoder import BatchRun, DeviceModel, ForwardRun, GreedyRunRecord, OracleError, run_greedy
 from .prefill import compare_gpu_logits, top1_non_eog
 
 __all__ = ["FaberError", "ModelConfig", "KvCacheLayout", "TINY", "LLAMA2_7B", "LLAMA3_70B",
-           "KV_F16", "KV_F32", "DeviceModel", "ForwardRun", "GreedyRunRecord", "OracleError",
+           "KV_F16", "KV_F32", "DeviceModel", "ForwardRun", "BatchRun", "GreedyRunRecord", "OracleError",
            "run_greedy", "compare_gpu_logits", "top1_non_eog", "lib"]
 
 

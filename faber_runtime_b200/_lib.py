@@ -94,6 +94,10 @@ SIGNATURES = {
     "faber_gpu_v2_session_last_greedy_ms": (Status, [P, ctypes.POINTER(ctypes.c_float)]),
     "faber_gpu_v2_session_commit": (Status, [P, I64, U32, U64, U64, ctypes.POINTER(I32)]),
     "faber_gpu_v2_nccl_unique_id": (Status, [P]),
+    "faber_gpu_v2_batch_open": (Status, [P, U32, PP]),
+    "faber_gpu_v2_batch_greedy": (Status, [P, U32, P, U32, P, P]),
+    "faber_gpu_v2_batch_last_ms": (Status, [P, ctypes.POINTER(ctypes.c_float)]),
+    "faber_gpu_v2_batch_close": (Status, [P]),
     "faber_gpu_v2_attention_decode_static": (Status, [P, P, P, P, U32, U32, U32, U64, P]),
     "faber_synth_q4k": (Status, [U64, U64, U64, P]),
     "faber_synth_normal_f32": (Status, [U64, U64, U64, ctypes.c_float, ctypes.c_float, P]),

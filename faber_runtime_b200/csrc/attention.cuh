@@ -45,7 +45,29 @@ struct AttnArgs {
   const StepState* st;
   int32_t n_heads, n_kv_heads, head_dim, max_splits;
   float scale;
+  // batched decode (grid.z = sequence): per-sequence state and this layer's
+  // K/V rows; q/ctx, part and counters advance by these strides per sequence
+  const SlotRef* slots;
+  int32_t slot_q_stride, slot_part_stride, slot_counter_stride;
 };
+
+// The arguments of sequence blockIdx.z of a batched launch (identity for a
+// single sequence).
+__device__ __forceinline__ AttnArgs slot_args(const AttnArgs& a0) {
+  AttnArgs a = a0;
+  if (a0.slots) {
+    const int z = blockIdx.z;
+    const SlotRef sl = a0.slots[z];
+    a.st = sl.st;
+    a.k = sl.k;
+    a.v = sl.v;
+    a.q = a0.q + (size_t)z * a0.slot_q_stride;
+    a.ctx = a0.ctx + (size_t)z * a0.slot_q_stride;
+    a.part = a0.part + (size_t)z * a0.slot_part_stride;
+    a.counters = a0.counters + (size_t)z * a0.slot_counter_stride;
+  }
+  return a;
+}
 
 // Splits per kv head for a session: about kAttnCtasPerSm CTAs per SM over all
 // kv heads, never more than the context has position groups.
@@ -205,7 +227,8 @@ __device__ __forceinline__ void kv_consume(const KvGroup<DPL>& g, int j0, int n_
 }
 
 template <int HD, int R>
-__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnArgs a0) {
+  const AttnArgs a = slot_args(a0);
   constexpr int DPL = HD / 32;
   static_assert(DPL == 2 || DPL == 4, "head_dim 64 or 128");
   __shared__ float pbuf[kAttnWarps][R][kAttnRows];

@@ -213,6 +213,7 @@ struct FaberGpuSession {
   faber::SessionState s;
 };
 
+
 namespace faber {
 
 // Decode attention with the smallest compiled group size (query heads per kv
@@ -870,11 +871,11 @@ inline TmapEncode tmap_encoder() {
 
 // Tensor map over the split activations [rows][K] f16: 64 x 256 boxes with the
 // 128-byte swizzle the UMMA B descriptor reads (rows past the end read 0).
-inline CUtensorMap xs_tensor_map(const __half* xs, uint64_t rows, uint64_t K) {
+inline CUtensorMap xs_tensor_map(const __half* xs, uint64_t rows, uint64_t K, int box_rows = kPgBN) {
   CUtensorMap map;
   const cuuint64_t dims[2] = {K, rows};
   const cuuint64_t strides[1] = {K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kPgBK, (cuuint32_t)kPgBN};
+  const cuuint32_t box[2] = {(cuuint32_t)kPgBK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = tmap_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(xs),
                                     dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -885,10 +886,11 @@ inline CUtensorMap xs_tensor_map(const __half* xs, uint64_t rows, uint64_t K) {
   return map;
 }
 
-template <int EPI>
+template <int EPI, int BN = kPgBN>
 void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGemmArgs a, int n_tok,
                          cudaStream_t stream) {
-  auto kern = prefill_gemm_kernel<EPI>;
+  auto kern = prefill_gemm_kernel<EPI, BN>;
+  constexpr int kPgSmemBytes = PgLayout<BN>::kBytes;
   static thread_local std::map<int, bool> attr_done;
   int dev = 0;
   FABER_CUDA(cudaGetDevice(&dev));
@@ -902,8 +904,8 @@ void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGe
   a.nb = W.nb;
   a.m_rows = W.rows;
   a.n_tok = n_tok;
-  const dim3 grid((2 * n_tok + kPgBN - 1) / kPgBN, (W.rows + kPgBM - 1) / kPgBM);
-  prefill_gemm_kernel<EPI><<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, a);
+  const dim3 grid((2 * n_tok + BN - 1) / BN, (W.rows + kPgBM - 1) / kPgBM);
+  kern<<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, a);
   FABER_CUDA(cudaGetLastError());
 }
 
@@ -1143,6 +1145,278 @@ inline void run_greedy(SessionState& S, uint32_t n_gen, const int64_t* eog, uint
   (void)M;
 }
 
+// ---------------------------------------------------------------------------
+// Batched greedy decode: up to kBatchMax sessions of one model advance one
+// token per step together. Every linear layer is one tcgen05 Q4_K GEMM whose
+// activation tile holds the sequences as (hi, lo) f16 column pairs, so each
+// weight byte is read once per step for the whole batch; attention runs per
+// sequence in one launch (grid.z = sequence) over each session's own cache.
+// The sessions keep their state: afterwards each holds its sequence's
+// residual, length and cache, and its own calls continue from there.
+// ---------------------------------------------------------------------------
+constexpr int kBatchMax = kPgBNSlots / 2;
+
+struct BatchState {
+  std::vector<SessionState*> seq;
+  int B = 0, device = 0, max_ctx = 0, splits = 0, gen_cap = 0;
+  cudaStream_t stream = nullptr;
+  DevBuf slots;  // SlotRef [L][B]
+  DevBuf h, xs, xscale, q, ctx, act, logits, attn_part, attn_counters, gen;
+  cudaGraphExec_t g_step = nullptr, g_logits = nullptr;
+  std::vector<int64_t> graph_eog;
+  bool graphs_valid = false;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  ~BatchState() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    if (g_step) cudaGraphExecDestroy(g_step);
+    if (g_logits) cudaGraphExecDestroy(g_logits);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    if (cur >= 0) cudaSetDevice(cur);
+  }
+};
+
+inline bool batch_supported(const ModelState& M) {
+  return prefill_supported(M) && !M.cfg.tied_head && M.head.identity;
+}
+
+inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
+  FABER_ARG(n >= 1 && n <= kBatchMax, "a batch holds 1 to " + std::to_string(kBatchMax) + " sessions");
+  SessionState& S0 = *seqs[0];
+  ModelState& M = S0.m->s;
+  require(batch_supported(M), FABER_STATUS_UNSUPPORTED,
+          "batched decode needs one GPU, an untied Q4_K head and dimensions in whole super-blocks");
+  for (int i = 0; i < n; ++i) {
+    FABER_ARG(seqs[i] != nullptr, "null session");
+    FABER_ARG(seqs[i]->m == S0.m, "every session of a batch must use the same model");
+    FABER_ARG(seqs[i]->max_ctx == S0.max_ctx, "every session of a batch must have the same context length");
+    FABER_ARG(!seqs[i]->trace, "traced sessions cannot join a batch");
+    for (int j = 0; j < i; ++j) FABER_ARG(seqs[j] != seqs[i], "a session appears twice in the batch");
+  }
+  const FaberModelConfigV1& c = M.cfg;
+  Bt.seq.assign(seqs, seqs + n);
+  Bt.B = n;
+  Bt.device = S0.device;
+  Bt.max_ctx = S0.max_ctx;
+  FABER_CUDA(cudaSetDevice(Bt.device));
+  FABER_CUDA(cudaStreamCreateWithFlags(&Bt.stream, cudaStreamNonBlocking));
+  FABER_CUDA(cudaEventCreate(&Bt.ev0));
+  FABER_CUDA(cudaEventCreate(&Bt.ev1));
+  const int d = (int)c.d_model, hd = (int)c.head_dim, nq = M.Hl * hd, nk = M.Hkvl * hd;
+  const size_t layer_cache = (size_t)Bt.max_ctx * nk;
+  std::vector<SlotRef> refs((size_t)c.n_layers * n);
+  for (uint32_t l = 0; l < c.n_layers; ++l)
+    for (int i = 0; i < n; ++i) {
+      SessionState& S = *seqs[i];
+      refs[(size_t)l * n + i] = SlotRef{st_ptr(S), S.kcache.as<__half>() + l * layer_cache,
+                                        S.vcache.as<__half>() + l * layer_cache};
+    }
+  Bt.slots.alloc(refs.size() * sizeof(SlotRef));
+  FABER_CUDA(cudaMemcpy(Bt.slots.p, refs.data(), Bt.slots.n, cudaMemcpyHostToDevice));
+  const size_t kmax = std::max((size_t)d, std::max((size_t)nq, (size_t)M.Fl));
+  Bt.h.alloc((size_t)n * d * 4);
+  // the activation tile always spans kPgBNSlots rows; rows past 2n stay zero
+  Bt.xs.alloc((size_t)kPgBNSlots * kmax * 2);
+  FABER_CUDA(cudaMemset(Bt.xs.p, 0, Bt.xs.n));
+  Bt.xscale.alloc((size_t)kBatchMax * 4);
+  FABER_CUDA(cudaMemset(Bt.xscale.p, 0, Bt.xscale.n));
+  Bt.q.alloc((size_t)n * nq * 4);
+  Bt.ctx.alloc((size_t)n * nq * 4);
+  Bt.act.alloc((size_t)n * M.Fl * 4);
+  Bt.logits.alloc((size_t)n * c.vocab * 4);
+  Bt.splits = attention_splits(device_info().sms, M.Hkvl * n, Bt.max_ctx);
+  Bt.attn_part.alloc((size_t)n * M.Hl * Bt.splits * (hd + 2) * 4);
+  Bt.attn_counters.alloc((size_t)n * M.Hkvl * 4);
+  FABER_CUDA(cudaMemset(Bt.attn_counters.p, 0, Bt.attn_counters.n));
+  Bt.gen_cap = Bt.max_ctx;
+  Bt.gen.alloc((size_t)n * Bt.gen_cap * 8);
+  (void)tmap_encoder();  // resolved before any graph capture
+}
+
+// The head over the batch's residual rows: logits, argmax keys, next tokens.
+inline void enqueue_batch_logits(BatchState& Bt, const std::vector<int64_t>& eog) {
+  ModelState& M = Bt.seq[0]->m->s;
+  const FaberModelConfigV1& c = M.cfg;
+  const int d = (int)c.d_model, n = Bt.B;
+  const SlotRef* sl0 = Bt.slots.as<SlotRef>();
+  __half* xs = Bt.xs.as<__half>();
+  prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.h.as<float>(), d, M.out_norm.as<float>(),
+                                                                 c.rms_eps, xs, Bt.xscale.as<float>());
+  PrefillGemmArgs a = {};
+  a.xscale = Bt.xscale.as<float>();
+  a.out = Bt.logits.as<float>();
+  a.ld_out = (int)c.vocab;
+  a.slots = sl0;
+  a.n_eog = (int)eog.size();
+  for (size_t i = 0; i < eog.size(); ++i) a.eog[i] = eog[i];
+  launch_prefill_gemm<PG_LOGITS, kPgBNSlots>(M.head, xs_tensor_map(xs, kPgBNSlots, d, kPgBNSlots), a, n,
+                                             Bt.stream);
+  slots_finalize_kernel<<<n, 32, 0, Bt.stream>>>(sl0, Bt.gen.as<int64_t>(), Bt.gen_cap);
+  FABER_CUDA(cudaGetLastError());
+}
+
+// One batched step: every sequence pushes its input token through all layers.
+inline void enqueue_batch_push(BatchState& Bt) {
+  ModelState& M = Bt.seq[0]->m->s;
+  SessionState& S0 = *Bt.seq[0];
+  const FaberModelConfigV1& c = M.cfg;
+  const int n = Bt.B, d = (int)c.d_model, hd = (int)c.head_dim, nq = M.Hl * hd, nk = M.Hkvl * hd;
+  const int F = M.Fl;
+  const SlotRef* sl = Bt.slots.as<SlotRef>();
+  float* H = Bt.h.as<float>();
+  __half* xs = Bt.xs.as<__half>();
+  float* xscale = Bt.xscale.as<float>();
+  const CUtensorMap map_d = xs_tensor_map(xs, kPgBNSlots, d, kPgBNSlots);
+  const CUtensorMap map_q = xs_tensor_map(xs, kPgBNSlots, nq, kPgBNSlots);
+  const CUtensorMap map_f = xs_tensor_map(xs, kPgBNSlots, F, kPgBNSlots);
+  slots_embed_kernel<<<n, 256, 0, Bt.stream>>>(sl, M.embd_f16.as<__half>(), d, (int)c.vocab, H);
+  FABER_CUDA(cudaGetLastError());
+  for (uint32_t l = 0; l < c.n_layers; ++l) {
+    LayerDev& L = M.layers[l];
+    const SlotRef* sll = sl + (size_t)l * n;
+    prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(H, d, L.attn_norm.as<float>(), c.rms_eps,
+                                                                   xs, xscale);
+    {
+      PrefillGemmArgs a = {};
+      a.xscale = xscale;
+      a.q_out = Bt.q.as<float>();
+      a.rope = S0.rope.as<float2>();
+      a.nq = nq;
+      a.nk = nk;
+      a.head_dim = hd;
+      a.slots = sll;
+      launch_prefill_gemm<PG_QKV_SLOTS, kPgBNSlots>(L.qkv, map_d, a, n, Bt.stream);
+    }
+    {
+      AttnArgs a = {};
+      a.q = Bt.q.as<float>();
+      a.ctx = Bt.ctx.as<float>();
+      a.part = Bt.attn_part.as<float>();
+      a.counters = Bt.attn_counters.as<int32_t>();
+      a.n_heads = M.Hl;
+      a.n_kv_heads = M.Hkvl;
+      a.head_dim = hd;
+      a.max_splits = Bt.splits;
+      a.scale = 1.0f / sqrtf((float)hd);
+      a.slots = sll;
+      a.slot_q_stride = nq;
+      a.slot_part_stride = M.Hl * Bt.splits * (hd + 2);
+      a.slot_counter_stride = M.Hkvl;
+      const dim3 grid(M.Hkvl, Bt.splits, n);
+      if (hd == 128)
+        launch_attention<128>(a, grid, Bt.stream, false);
+      else
+        launch_attention<64>(a, grid, Bt.stream, false);
+    }
+    prefill_split_kernel<false><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.ctx.as<float>(), nq, nullptr, 0.0f,
+                                                                    xs, xscale);
+    {
+      PrefillGemmArgs a = {};
+      a.xscale = xscale;
+      a.out = H;
+      a.ld_out = d;
+      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.o, map_q, a, n, Bt.stream);
+    }
+    prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(H, d, L.ffn_norm.as<float>(), c.rms_eps,
+                                                                   xs, xscale);
+    {
+      PrefillGemmArgs a = {};
+      a.xscale = xscale;
+      a.out = Bt.act.as<float>();
+      a.ld_out = F;
+      launch_prefill_gemm<PG_SWIGLU, kPgBNSlots>(L.gateup, map_d, a, n, Bt.stream);
+    }
+    prefill_split_kernel<false><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.act.as<float>(), F, nullptr, 0.0f,
+                                                                    xs, xscale);
+    {
+      PrefillGemmArgs a = {};
+      a.xscale = xscale;
+      a.out = H;
+      a.ld_out = d;
+      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.down, map_f, a, n, Bt.stream);
+    }
+    FABER_CUDA(cudaGetLastError());
+  }
+}
+
+inline void batch_graphs(BatchState& Bt, const std::vector<int64_t>& eog) {
+  if (Bt.graphs_valid && Bt.graph_eog == eog) return;
+  if (Bt.g_step) cudaGraphExecDestroy(Bt.g_step);
+  if (Bt.g_logits) cudaGraphExecDestroy(Bt.g_logits);
+  Bt.g_step = Bt.g_logits = nullptr;
+  cudaGraph_t g;
+  FABER_CUDA(cudaStreamBeginCapture(Bt.stream, cudaStreamCaptureModeThreadLocal));
+  enqueue_batch_logits(Bt, eog);
+  FABER_CUDA(cudaStreamEndCapture(Bt.stream, &g));
+  FABER_CUDA(cudaGraphInstantiate(&Bt.g_logits, g, 0));
+  FABER_CUDA(cudaGraphDestroy(g));
+  FABER_CUDA(cudaStreamBeginCapture(Bt.stream, cudaStreamCaptureModeThreadLocal));
+  enqueue_batch_push(Bt);
+  enqueue_batch_logits(Bt, eog);
+  FABER_CUDA(cudaStreamEndCapture(Bt.stream, &g));
+  FABER_CUDA(cudaGraphInstantiate(&Bt.g_step, g, 0));
+  FABER_CUDA(cudaGraphDestroy(g));
+  Bt.graph_eog = eog;
+  Bt.graphs_valid = true;
+}
+
+// run_greedy (src/greedy_run.rs:186-248) for every sequence of the batch at
+// once: n_gen tokens each, out[i * n_gen + j] = token j of sequence i.
+inline void run_batch_greedy(BatchState& Bt, uint32_t n_gen, const int64_t* eog, uint32_t n_eog,
+                             int64_t* out, int32_t* all_finite) {
+  FABER_CUDA(cudaSetDevice(Bt.device));
+  FABER_ARG(n_eog <= (uint32_t)kMaxEog, "at most 8 EOG ids");
+  FABER_ARG(out != nullptr || n_gen == 0, "null output");
+  if (n_gen == 0) return;
+  FABER_ARG(n_gen <= (uint32_t)Bt.gen_cap, "n_gen above the context length");
+  ModelState& M = Bt.seq[0]->m->s;
+  const size_t d = M.cfg.d_model;
+  for (int i = 0; i < Bt.B; ++i) {
+    SessionState& S = *Bt.seq[i];
+    FABER_ARG(S.n > 0, "greedy decode needs a prompt in every session");
+    require(S.n + n_gen - 1 <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
+    check_prefix_complete(S);
+    // the session's own work has finished before the batch stream reads it
+    FABER_CUDA(cudaStreamSynchronize(S.stream));
+    StepState st;
+    FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+    st.gen_count = 0;
+    st.finite = 1;
+    st.argmax_key = 0;
+    FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
+    FABER_CUDA(cudaMemcpyAsync(Bt.h.as<float>() + (size_t)i * d, S.h.p, d * 4, cudaMemcpyDeviceToDevice,
+                               Bt.stream));
+  }
+  std::vector<int64_t> e(eog, eog + n_eog);
+  batch_graphs(Bt, e);
+  FABER_CUDA(cudaEventRecord(Bt.ev0, Bt.stream));
+  FABER_CUDA(cudaGraphLaunch(Bt.g_logits, Bt.stream));
+  for (uint32_t j = 1; j < n_gen; ++j) FABER_CUDA(cudaGraphLaunch(Bt.g_step, Bt.stream));
+  FABER_CUDA(cudaEventRecord(Bt.ev1, Bt.stream));
+  std::vector<int64_t> gen((size_t)Bt.B * Bt.gen_cap);
+  FABER_CUDA(cudaMemcpyAsync(gen.data(), Bt.gen.p, Bt.gen.n, cudaMemcpyDeviceToHost, Bt.stream));
+  for (int i = 0; i < Bt.B; ++i)  // each session continues from its sequence's residual
+    FABER_CUDA(cudaMemcpyAsync(Bt.seq[i]->h.p, Bt.h.as<float>() + (size_t)i * d, d * 4,
+                               cudaMemcpyDeviceToDevice, Bt.stream));
+  FABER_CUDA(cudaStreamSynchronize(Bt.stream));
+  check_device_waits();
+  FABER_CUDA(cudaEventElapsedTime(&Bt.last_ms, Bt.ev0, Bt.ev1));
+  for (int i = 0; i < Bt.B; ++i) {
+    SessionState& S = *Bt.seq[i];
+    StepState st;
+    FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+    require(st.status == 0, FABER_STATUS_KERNEL_ERROR, "device-side token check failed");
+    if (all_finite) all_finite[i] = st.finite;
+    for (uint32_t j = 0; j < n_gen; ++j) out[(size_t)i * n_gen + j] = gen[(size_t)i * Bt.gen_cap + j];
+    S.n += n_gen - 1;
+  }
+}
+
 inline void set_prefix(SessionState& S, uint32_t layer, const float* k, const float* v, uint64_t n) {
   ModelState& M = S.m->s;
   const FaberModelConfigV1& c = M.cfg;
@@ -1347,6 +1621,53 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_greedy(FaberGpuSession* s, uin
     FABER_ARG(s && (eog || n_eog == 0), "null pointer");
     run_greedy(s->s, n_gen, eog, n_eog, out_tokens, all_finite);
   });
+}
+
+struct FaberGpuBatch {
+  faber::BatchState b;
+};
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_batch_open(FaberGpuSession* const* sessions, uint32_t n,
+                                                    FaberGpuBatch** out) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_batch_open", [&] {
+    FABER_ARG(sessions && out, "null pointer");
+    *out = nullptr;
+    FABER_ARG(n >= 1 && n <= (uint32_t)kBatchMax,
+              "a batch holds 1 to " + std::to_string(kBatchMax) + " sessions");
+    std::vector<SessionState*> seqs(n);
+    for (uint32_t i = 0; i < n; ++i) {
+      FABER_ARG(sessions[i] != nullptr, "null session");
+      seqs[i] = &sessions[i]->s;
+    }
+    auto b = std::make_unique<FaberGpuBatch>();
+    batch_build(b->b, seqs.data(), (int)n);
+    *out = b.release();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_batch_greedy(FaberGpuBatch* b, uint32_t n_gen, const int64_t* eog,
+                                                      uint32_t n_eog, int64_t* out_tokens,
+                                                      int32_t* all_finite) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_batch_greedy", [&] {
+    FABER_ARG(b, "null batch");
+    FABER_ARG(eog != nullptr || n_eog == 0, "null EOG list");
+    run_batch_greedy(b->b, n_gen, eog, n_eog, out_tokens, all_finite);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_batch_last_ms(const FaberGpuBatch* b, float* ms) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_batch_last_ms", [&] {
+    FABER_ARG(b && ms, "null pointer");
+    *ms = b->b.last_ms;
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_batch_close(FaberGpuBatch* b) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_batch_close", [&] { delete b; });
 }
 
 FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_set_prefix(FaberGpuSession* s, uint32_t layer,

@@ -108,6 +108,14 @@ struct StepState {
   unsigned long long argmax_key;
 };
 
+// One sequence of a batched decode step: its step state and this layer's
+// K/V cache rows ([ctx][Hkv*hd] f16).
+struct SlotRef {
+  StepState* st;
+  __half* k;
+  __half* v;
+};
+
 // embed_rows (src/cpu_oracle.rs:538-545) with the f16-rounded token_embd
 // stored as f16; also opens the step: cur_pos = n, n += 1.
 __global__ void embed_kernel(StepState* st, const __half* __restrict__ embd, int d, int vocab,
@@ -138,6 +146,45 @@ __global__ void finalize_kernel(StepState* st, int64_t* gen, int32_t gen_cap) {
   const int32_t c = st->gen_count;
   if (gen && c >= 0 && c < gen_cap) {
     gen[c] = tok;
+    st->gen_count = c + 1;
+  }
+  st->argmax_key = 0ull;
+}
+
+// Batched decode: embed_kernel for sequence blockIdx.x (its step state,
+// row blockIdx.x of h).
+__global__ void slots_embed_kernel(const SlotRef* slots, const __half* __restrict__ embd, int d,
+                                   int vocab, float* __restrict__ h) {
+  pdl_wait();
+  pdl_launch_dependents();
+  StepState* st = slots[blockIdx.x].st;
+  const int64_t tok = st->input_token;
+  const bool ok = tok >= 0 && tok < vocab;
+  float* hr = h + (size_t)blockIdx.x * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    hr[i] = ok ? __half2float(embd[(size_t)tok * d + i]) : 0.0f;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!ok) st->status = 1;
+    st->cur_pos = st->n;
+    st->n = st->n + 1;
+    st->argmax_key = 0ull;
+  }
+}
+
+// Batched decode: finalize_kernel for sequence blockIdx.x; its greedy ids go
+// to gen[blockIdx.x * gen_cap ..].
+__global__ void slots_finalize_kernel(const SlotRef* slots, int64_t* gen, int32_t gen_cap) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x != 0) return;
+  StepState* st = slots[blockIdx.x].st;
+  const unsigned long long key = st->argmax_key;
+  const int64_t tok = key ? (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffull)) : 0;
+  st->input_token = tok;
+  const int32_t c = st->gen_count;
+  if (gen && c >= 0 && c < gen_cap) {
+    gen[(size_t)blockIdx.x * gen_cap + c] = tok;
     st->gen_count = c + 1;
   }
   st->argmax_key = 0ull;

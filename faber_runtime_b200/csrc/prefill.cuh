@@ -32,33 +32,44 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "ops.cuh"
 
 namespace faber {
 
 constexpr int kPgBM = 128;
-constexpr int kPgBN = 256;
+constexpr int kPgBN = 256;       // activation columns per tile in the prompt pass (128 tokens)
+constexpr int kPgBNSlots = 32;   // ... in batched decode (up to 16 sequences)
 constexpr int kPgBK = 64;
 constexpr int kPgAStages = 6;    // dequantized weight tiles in flight
 constexpr int kPgBStages = 4;    // activation tiles in flight
 constexpr int kPgThreads = 320;  // warp 0 loads, warp 1 MMA, warps 2-9 dequant + epilogue
 constexpr int kPgDequantWarps = 8;
 constexpr int kPgATile = kPgBM * kPgBK * 2;                         // 16 KB
-constexpr int kPgBTile = kPgBN * kPgBK * 2;                         // 32 KB
-constexpr int kPgSmemA = 0;
-constexpr int kPgSmemB = kPgSmemA + kPgAStages * kPgATile;          // 96 KB
-constexpr int kPgSmemBars = kPgSmemB + kPgBStages * kPgBTile;       // 224 KB
-constexpr int kPgSmemXs = kPgSmemBars + 256;                         // 128 token row scales
-constexpr int kPgSmemBytes = kPgSmemXs + (kPgBN / 2) * 4 + 1024;     // + alignment slack
-static_assert(kPgSmemBytes <= 227 * 1024, "prefill GEMM shared memory above the per-CTA limit");
-static_assert((2 * kPgAStages + 2 * kPgBStages + 1) * 8 + 4 <= 256, "barrier area");
-static_assert(kPgSmemB % 1024 == 0, "128-byte-swizzled tiles start on 1024-byte boundaries");
+
+// Shared-memory layout for an activation tile of BN columns (hi/lo rows).
+template <int BN>
+struct PgLayout {
+  static constexpr int kBTile = BN * kPgBK * 2;                     // 32 KB at 256 columns
+  static constexpr int kSmemA = 0;
+  static constexpr int kSmemB = kSmemA + kPgAStages * kPgATile;     // 96 KB
+  static constexpr int kSmemBars = kSmemB + kPgBStages * kBTile;
+  static constexpr int kSmemXs = kSmemBars + 256;                    // BN/2 token row scales
+  static constexpr int kBytes = kSmemXs + (BN / 2) * 4 + 1024;       // + alignment slack
+  static_assert(kBytes <= 227 * 1024, "prefill GEMM shared memory above the per-CTA limit");
+  static_assert((2 * kPgAStages + 2 * kPgBStages + 1) * 8 + 4 <= 256, "barrier area");
+  static_assert(kSmemB % 1024 == 0 && kBTile % 1024 == 0,
+                "128-byte-swizzled tiles start on 1024-byte boundaries");
+  static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "TMEM columns: a power of two");
+};
 
 // Epilogues of the prefill GEMM (per output element y[t][m]).
 enum PrefillEpi : int {
   PG_STORE = 0,   // out[t][m] = y
   PG_RESID = 1,   // out[t][m] += y (residual_add, src/decoder_ops.rs:420-427)
   PG_SWIGLU = 2,  // rows interleaved gate/up: out[t][m/2] = silu(g) * u
-  PG_QKV = 3      // RoPE on Q/K pairs, Q -> q_out[t], K/V -> f16 cache at position pos0 + t
+  PG_QKV = 3,     // RoPE on Q/K pairs, Q -> q_out[t], K/V -> f16 cache at position pos0 + t
+  PG_QKV_SLOTS = 4,  // batched decode: token t is sequence t, at its own position and cache
+  PG_LOGITS = 5      // batched decode: logits row t, argmax key and finite flag of sequence t
 };
 
 struct PrefillGemmArgs {
@@ -75,6 +86,10 @@ struct PrefillGemmArgs {
   __half* v_cache;
   const float2* rope;      // [ctx][head_dim/2]
   int32_t nq, nk, head_dim, pos0;
+  // PG_QKV_SLOTS / PG_LOGITS: sequence t's state and this layer's K/V rows
+  const SlotRef* slots;
+  int32_t n_eog;           // PG_LOGITS: ids excluded from the argmax
+  int64_t eog[kMaxEog];
 };
 
 // ---- tcgen05 / TMA helpers ------------------------------------------------
@@ -145,10 +160,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive f32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // ---- the kernel -----------------------------------------------------------
-template <int EPI>
+template <int EPI, int BN>
 __global__ void __launch_bounds__(kPgThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ CUtensorMap xs_map, const PrefillGemmArgs a) {
+  using Lay = PgLayout<BN>;
+  constexpr int kPgSmemA = Lay::kSmemA, kPgSmemB = Lay::kSmemB, kPgSmemBars = Lay::kSmemBars;
+  constexpr int kPgSmemXs = Lay::kSmemXs, kPgBTile = Lay::kBTile;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -168,8 +201,8 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   // its Q4_K bytes come from DRAM once and from L2 for the others
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
   const int nkb = a.nb * (256 / kPgBK);  // K steps
-  if (threadIdx.x < kPgBN / 2) {
-    const int t = n_tile * (kPgBN / 2) + threadIdx.x;
+  if (threadIdx.x < BN / 2) {
+    const int t = n_tile * (BN / 2) + threadIdx.x;
     xs_s[threadIdx.x] = t < a.n_tok ? a.xscale[t] : 0.0f;
   }
   if (threadIdx.x == 0) {
@@ -187,7 +220,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
-                 "r"(kPgBN));
+                 "r"(BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -201,12 +234,12 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         const int s = kb % kPgBStages;
         if (kb >= kPgBStages) mbar_wait(&b_empty[s], ((kb / kPgBStages) - 1) & 1);
         mbar_arrive_expect_tx(&b_full[s], (uint32_t)kPgBTile);
-        tma_load_2d(sb + s * kPgBTile, &xs_map, kb * kPgBK, n_tile * kPgBN, &b_full[s]);
+        tma_load_2d(sb + s * kPgBTile, &xs_map, kb * kPgBK, n_tile * BN, &b_full[s]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_f16(kPgBM, kPgBN);
+      const uint32_t idesc = umma_idesc_f16(kPgBM, BN);
       for (int kb = 0; kb < nkb; ++kb) {
         const int sa_i = kb % kPgAStages, sb_i = kb % kPgBStages;
         mbar_wait(&a_full[sa_i], (kb / kPgAStages) & 1);
@@ -300,27 +333,31 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     tc_fence_after();
     const int quad = warp & 3;
     const int m = m_tile * kPgBM + quad * 32 + lane;
-    const int cbeg = half * (kPgBN / 2);
+    const int cbeg = half * (BN / 2);
     const bool row_ok = m < a.m_rows;
-    for (int c0 = cbeg; c0 < cbeg + kPgBN / 2; c0 += 32) {
-      float v[32];
-      tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
-      const int tb = (n_tile * kPgBN + c0) / 2;  // first token of these 16 column pairs
-      float y[16];
+    constexpr int CW = BN / 2 < 32 ? BN / 2 : 32;  // columns per TMEM read
+    constexpr int TPC = CW / 2;                    // tokens per TMEM read
+    for (int c0 = cbeg; c0 < cbeg + BN / 2; c0 += CW) {
+      float v[CW];
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
+      if constexpr (CW == 32) tmem_ld32(taddr, v);
+      else tmem_ld16(taddr, v);
+      const int tb = (n_tile * BN + c0) / 2;  // first token of these column pairs
+      float y[TPC];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) y[j] = (v[2 * j] + v[2 * j + 1]) * xs_s[c0 / 2 + j];
+      for (int j = 0; j < TPC; ++j) y[j] = (v[2 * j] + v[2 * j + 1]) * xs_s[c0 / 2 + j];
       // every load of a chunk is issued before its stores
       if (EPI == PG_STORE) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < TPC; ++j)
           if (tb + j < a.n_tok && row_ok) a.out[(size_t)(tb + j) * a.ld_out + m] = y[j];
       } else if (EPI == PG_RESID) {
-        float old[16];
+        float old[TPC];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < TPC; ++j)
           old[j] = (tb + j < a.n_tok && row_ok) ? a.out[(size_t)(tb + j) * a.ld_out + m] : 0.0f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < TPC; ++j)
           if (tb + j < a.n_tok && row_ok) a.out[(size_t)(tb + j) * a.ld_out + m] = old[j] + y[j];
       } else if (EPI == PG_SWIGLU) {
         // rows 2f (gate) and 2f+1 (up) sit in adjacent lanes; of each token
@@ -328,7 +365,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         // second, each taking the partner row's value by one shuffle
         const bool odd = (lane & 1) != 0;
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < TPC / 2; ++jj) {
           const float mine = odd ? y[2 * jj + 1] : y[2 * jj];
           const float other = __shfl_xor_sync(0xffffffffu, odd ? y[2 * jj] : y[2 * jj + 1], 1);
           const float g = odd ? other : mine, u = odd ? mine : other;
@@ -338,21 +375,27 @@ __global__ void __launch_bounds__(kPgThreads, 1)
             a.out[(size_t)t * a.ld_out + (m >> 1)] = __fmul_rn(sg, u);
           }
         }
-      } else {  // PG_QKV
+      } else if (EPI == PG_QKV || EPI == PG_QKV_SLOTS) {
         const bool rope = m < a.nq + a.nk;  // Q and K rows (warp-uniform: head-aligned)
         const int kk = (m % a.head_dim) >> 1;
-        float2 cs[16];
+        int pos[TPC];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          cs[j] = (rope && tb + j < a.n_tok)
-                      ? a.rope[(size_t)(a.pos0 + tb + j) * (a.head_dim >> 1) + kk]
-                      : make_float2(0.0f, 0.0f);
+        for (int j = 0; j < TPC; ++j) {
+          if (EPI == PG_QKV) pos[j] = a.pos0 + tb + j;
+          else pos[j] = tb + j < a.n_tok ? a.slots[tb + j].st->cur_pos : 0;
+        }
+        float2 cs[TPC];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < TPC; ++j)
+          cs[j] = (rope && tb + j < a.n_tok) ? a.rope[(size_t)pos[j] * (a.head_dim >> 1) + kk]
+                                             : make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < TPC; ++j) {
           const float y1 = __shfl_xor_sync(0xffffffffu, y[j], 1);
           const int t = tb + j;
           if (t < a.n_tok && row_ok) {
-            const int pos = a.pos0 + t;
+            __half* kc = EPI == PG_QKV ? a.k_cache : a.slots[t].k;
+            __half* vc = EPI == PG_QKV ? a.v_cache : a.slots[t].v;
             if (rope) {
               // rope_norm pair (m even: first, odd: second) with host cos/sin
               const bool first = (m & 1) == 0;
@@ -360,10 +403,34 @@ __global__ void __launch_bounds__(kPgThreads, 1)
               const float o = first ? __fsub_rn(__fmul_rn(x0, cs[j].x), __fmul_rn(x1, cs[j].y))
                                     : __fadd_rn(__fmul_rn(x0, cs[j].y), __fmul_rn(x1, cs[j].x));
               if (m < a.nq) a.q_out[(size_t)t * a.nq + m] = o;
-              else a.k_cache[(size_t)pos * a.nk + (m - a.nq)] = __float2half_rn(o);
+              else kc[(size_t)pos[j] * a.nk + (m - a.nq)] = __float2half_rn(o);
             } else {
-              a.v_cache[(size_t)pos * a.nk + (m - a.nq - a.nk)] = __float2half_rn(y[j]);
+              vc[(size_t)pos[j] * a.nk + (m - a.nq - a.nk)] = __float2half_rn(y[j]);
             }
+          }
+        }
+      } else {  // PG_LOGITS: top1_non_eog (src/cpu_oracle.rs:979-995) per sequence
+        bool eog = false;
+        for (int e = 0; e < a.n_eog; ++e) eog |= (a.eog[e] == (int64_t)m);
+#pragma unroll
+        for (int j = 0; j < TPC; ++j) {
+          const int t = tb + j;
+          const bool live = t < a.n_tok && row_ok;
+          if (live) a.out[(size_t)t * a.ld_out + m] = y[j];
+          // strict '>' from -inf: NaN and -inf never win, the lowest id wins ties
+          unsigned long long key = 0ull;
+          if (live && !eog && y[j] > -INFINITY)
+            key = ((unsigned long long)ordered_bits(y[j]) << 32) | (0xffffffffu - (uint32_t)m);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other > key ? other : key;
+          }
+          const bool bad = __any_sync(0xffffffffu, live && !isfinite(y[j]));
+          if (lane == 0 && t < a.n_tok) {
+            StepState* st = a.slots[t].st;
+            if (key) atomicMax(&st->argmax_key, key);
+            if (bad) atomicAnd(&st->finite, 0);
           }
         }
       }
@@ -373,7 +440,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPgBN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
   }
 }
 

@@ -181,6 +181,45 @@ class ForwardRun:
         return "idempotent_replay" if out.value == 1 else "applied"
 
 
+class BatchRun:
+    """Batched greedy decode over open ForwardRuns of one model: every step
+    reads each weight once for all sequences (up to 16), and each run keeps
+    its own sequence state afterwards (its next call continues from there)."""
+
+    def __init__(self, runs):
+        self.runs = list(runs)
+        arr = (ctypes.c_void_p * len(self.runs))(*[r._h.value for r in self.runs])
+        h = ctypes.c_void_p()
+        _lib.call("faber_gpu_v2_batch_open", ctypes.addressof(arr), len(self.runs), ctypes.byref(h))
+        self._h = h
+
+    def greedy(self, n_gen: int, eog=()) -> tuple[np.ndarray, np.ndarray]:
+        """Tokens [n_runs][n_gen] and the per-run finite gate."""
+        n = len(self.runs)
+        out = np.empty((n, max(n_gen, 1)), np.int64)
+        fin = np.ones(n, np.int32)
+        e = np.ascontiguousarray(list(eog) or [0], np.int64)
+        _lib.call("faber_gpu_v2_batch_greedy", self._h, n_gen, e.ctypes.data, len(eog),
+                  out.ctypes.data, fin.ctypes.data)
+        return out[:, :n_gen].copy(), fin.astype(bool)
+
+    def last_ms(self) -> float:
+        ms = ctypes.c_float()
+        _lib.call("faber_gpu_v2_batch_last_ms", self._h, ctypes.byref(ms))
+        return ms.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.call("faber_gpu_v2_batch_close", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 @dataclass
 class GreedyDivergence:
     position: int

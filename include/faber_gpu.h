@@ -55,6 +55,7 @@ enum {
 
 typedef struct FaberGpuModel FaberGpuModel;
 typedef struct FaberGpuSession FaberGpuSession;
+typedef struct FaberGpuBatch FaberGpuBatch;
 
 /* ------------------------------------------------------------------------
  * Library / diagnostics
@@ -233,6 +234,26 @@ FaberRtStatusV1 faber_gpu_v2_session_position_logits(FaberGpuSession* s, float* 
 FaberRtStatusV1 faber_gpu_v2_session_greedy(FaberGpuSession* s, uint32_t n_gen,
                                             const int64_t* eog, uint32_t n_eog,
                                             int64_t* out_tokens, int32_t* all_finite);
+/* Batched greedy decode — run_greedy (src/greedy_run.rs:186-248) for up to
+ * 16 sequences in lockstep, the batch-16 decode of the reference's
+ * multi-sequence KvCacheLayout (src/kv_cache.rs:504-626, `slots`). The batch
+ * is a view over n open sessions of one model (same context length, one
+ * GPU, untied Q4_K head, dimensions in whole super-blocks): each session
+ * holds one sequence with its prompt already pushed. Every linear layer
+ * reads its weights once per step for all sequences. The sessions stay
+ * usable: after batch_greedy each holds its sequence's state, exactly as if
+ * session_greedy had run on it. Unsupported models give UNSUPPORTED. */
+FaberRtStatusV1 faber_gpu_v2_batch_open(FaberGpuSession* const* sessions, uint32_t n,
+                                        FaberGpuBatch** out);
+/* n_gen greedy tokens per sequence: out_tokens[i * n_gen + j] is token j of
+ * sequence i; all_finite[i] (optional, n entries) its finite gate. The EOG
+ * ids are excluded from every argmax, as in session_greedy. */
+FaberRtStatusV1 faber_gpu_v2_batch_greedy(FaberGpuBatch* b, uint32_t n_gen, const int64_t* eog,
+                                          uint32_t n_eog, int64_t* out_tokens,
+                                          int32_t* all_finite);
+/* Device time of the last batch_greedy (CUDA events around its steps). */
+FaberRtStatusV1 faber_gpu_v2_batch_last_ms(const FaberGpuBatch* b, float* ms);
+FaberRtStatusV1 faber_gpu_v2_batch_close(FaberGpuBatch* b);
 /* Install a K/V prefix of n positions for one layer (host f32 [n][kv_heads*
  * head_dim]; stored f16-rounded like every cached value). All layers must be
  * given the same n before the next push. */
