@@ -888,7 +888,7 @@ inline CUtensorMap xs_tensor_map(const __half* xs, uint64_t rows, uint64_t K, in
 
 template <int EPI, int BN = kPgBN>
 void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGemmArgs a, int n_tok,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, int k_splits = 1) {
   auto kern = prefill_gemm_kernel<EPI, BN>;
   constexpr int kPgSmemBytes = PgLayout<BN>::kBytes;
   static thread_local std::map<int, bool> attr_done;
@@ -904,7 +904,12 @@ void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGe
   a.nb = W.nb;
   a.m_rows = W.rows;
   a.n_tok = n_tok;
-  const dim3 grid((2 * n_tok + BN - 1) / BN, (W.rows + kPgBM - 1) / kPgBM);
+  if (k_splits > 1) {
+    a.k_chunk = (W.nb + k_splits - 1) / k_splits;
+    k_splits = (W.nb + a.k_chunk - 1) / a.k_chunk;  // no empty split
+    require(a.part != nullptr && a.tile_cnt != nullptr, FABER_STATUS_UNSUPPORTED, "split K without scratch");
+  }
+  const dim3 grid((2 * n_tok + BN - 1) / BN, (W.rows + kPgBM - 1) / kPgBM, std::max(1, k_splits));
   kern<<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, a);
   FABER_CUDA(cudaGetLastError());
 }
@@ -1162,6 +1167,7 @@ struct BatchState {
   cudaStream_t stream = nullptr;
   DevBuf slots;  // SlotRef [L][B]
   DevBuf h, xs, xscale, q, ctx, act, logits, attn_part, attn_counters, gen;
+  DevBuf kpart, tile_cnt;  // split-K partial tiles and per-tile tickets
   cudaGraphExec_t g_step = nullptr, g_logits = nullptr;
   std::vector<int64_t> graph_eog;
   bool graphs_valid = false;
@@ -1180,6 +1186,18 @@ struct BatchState {
     if (cur >= 0) cudaSetDevice(cur);
   }
 };
+
+// K splits for a batched-decode GEMM: as many as keep the grid within one
+// wave (one CTA per SM) when the weight has fewer 128-row tiles than SMs (at
+// most 8 splits, whole super-blocks).
+inline int batch_k_splits(const DeviceTiled& W) {
+  const int m_tiles = (W.rows + kPgBM - 1) / kPgBM;
+  const int sms = device_info().sms;
+  if (2 * m_tiles > sms) return 1;
+  const int want = std::min(std::min(8, W.nb), sms / m_tiles);
+  const int chunk = (W.nb + want - 1) / want;
+  return (W.nb + chunk - 1) / chunk;
+}
 
 inline bool batch_supported(const ModelState& M) {
   return prefill_supported(M) && !M.cfg.tied_head && M.head.identity;
@@ -1235,6 +1253,23 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   FABER_CUDA(cudaMemset(Bt.attn_counters.p, 0, Bt.attn_counters.n));
   Bt.gen_cap = Bt.max_ctx;
   Bt.gen.alloc((size_t)n * Bt.gen_cap * 8);
+  size_t part = 0, tiles = 0;
+  auto need = [&](const DeviceTiled& W) {
+    const size_t m_tiles = (W.rows + kPgBM - 1) / kPgBM;
+    const int sp = batch_k_splits(W);
+    if (sp > 1) part = std::max(part, m_tiles * sp * kPgBM * kPgBNSlots);
+    tiles = std::max(tiles, m_tiles);
+  };
+  for (const LayerDev& L : M.layers) {
+    need(L.qkv);
+    need(L.o);
+    need(L.gateup);
+    need(L.down);
+  }
+  need(M.head);
+  Bt.kpart.alloc(std::max<size_t>(part, 1) * 4);
+  Bt.tile_cnt.alloc(tiles * 4);
+  FABER_CUDA(cudaMemset(Bt.tile_cnt.p, 0, Bt.tile_cnt.n));
   (void)tmap_encoder();  // resolved before any graph capture
 }
 
@@ -1254,8 +1289,10 @@ inline void enqueue_batch_logits(BatchState& Bt, const std::vector<int64_t>& eog
   a.slots = sl0;
   a.n_eog = (int)eog.size();
   for (size_t i = 0; i < eog.size(); ++i) a.eog[i] = eog[i];
+  a.part = Bt.kpart.as<float>();
+  a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
   launch_prefill_gemm<PG_LOGITS, kPgBNSlots>(M.head, xs_tensor_map(xs, kPgBNSlots, d, kPgBNSlots), a, n,
-                                             Bt.stream);
+                                             Bt.stream, batch_k_splits(M.head));
   slots_finalize_kernel<<<n, 32, 0, Bt.stream>>>(sl0, Bt.gen.as<int64_t>(), Bt.gen_cap);
   FABER_CUDA(cudaGetLastError());
 }
@@ -1290,7 +1327,9 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.nk = nk;
       a.head_dim = hd;
       a.slots = sll;
-      launch_prefill_gemm<PG_QKV_SLOTS, kPgBNSlots>(L.qkv, map_d, a, n, Bt.stream);
+      a.part = Bt.kpart.as<float>();
+      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
+      launch_prefill_gemm<PG_QKV_SLOTS, kPgBNSlots>(L.qkv, map_d, a, n, Bt.stream, batch_k_splits(L.qkv));
     }
     {
       AttnArgs a = {};
@@ -1320,7 +1359,9 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.xscale = xscale;
       a.out = H;
       a.ld_out = d;
-      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.o, map_q, a, n, Bt.stream);
+      a.part = Bt.kpart.as<float>();
+      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
+      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.o, map_q, a, n, Bt.stream, batch_k_splits(L.o));
     }
     prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(H, d, L.ffn_norm.as<float>(), c.rms_eps,
                                                                    xs, xscale);
@@ -1329,7 +1370,9 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.xscale = xscale;
       a.out = Bt.act.as<float>();
       a.ld_out = F;
-      launch_prefill_gemm<PG_SWIGLU, kPgBNSlots>(L.gateup, map_d, a, n, Bt.stream);
+      a.part = Bt.kpart.as<float>();
+      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
+      launch_prefill_gemm<PG_SWIGLU, kPgBNSlots>(L.gateup, map_d, a, n, Bt.stream, batch_k_splits(L.gateup));
     }
     prefill_split_kernel<false><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.act.as<float>(), F, nullptr, 0.0f,
                                                                     xs, xscale);
@@ -1338,7 +1381,9 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.xscale = xscale;
       a.out = H;
       a.ld_out = d;
-      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.down, map_f, a, n, Bt.stream);
+      a.part = Bt.kpart.as<float>();
+      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
+      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.down, map_f, a, n, Bt.stream, batch_k_splits(L.down));
     }
     FABER_CUDA(cudaGetLastError());
   }

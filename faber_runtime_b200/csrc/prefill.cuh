@@ -90,6 +90,12 @@ struct PrefillGemmArgs {
   const SlotRef* slots;
   int32_t n_eog;           // PG_LOGITS: ids excluded from the argmax
   int64_t eog[kMaxEog];
+  // split K (grid.z > 1): super-block columns per split; each split's 128 x BN
+  // partial tile goes to part, and the split that finishes a tile last sums
+  // the partials in split order and runs the epilogue
+  int32_t k_chunk;
+  float* part;             // [m_tiles][n_tiles][splits][128][BN]
+  unsigned int* tile_cnt;  // [m_tiles][n_tiles], zero between launches
 };
 
 // ---- tcgen05 / TMA helpers ------------------------------------------------
@@ -175,6 +181,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 consecutive f32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[CW]) {
+  if constexpr (CW == 32) tmem_ld32(taddr, v);
+  else if constexpr (CW == 16) tmem_ld16(taddr, v);
+  else tmem_ld8(taddr, v);
+}
+
 // ---- the kernel -----------------------------------------------------------
 template <int EPI, int BN>
 __global__ void __launch_bounds__(kPgThreads, 1)
@@ -194,13 +219,19 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   uint64_t* a_empty = a_full + kPgAStages;     // [kPgAStages] MMAs reading it finished
   uint64_t* tile_done = a_empty + kPgAStages;  // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_done + 1);
+  int* last_split = reinterpret_cast<int*>(tmem_slot + 1);
   float* xs_s = reinterpret_cast<float*>(smem + kPgSmemXs);  // row scales of this tile's tokens
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the column tiles of one weight tile are neighbours in launch order, so
   // its Q4_K bytes come from DRAM once and from L2 for the others
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  const int nkb = a.nb * (256 / kPgBK);  // K steps
+  // this CTA's super-block columns [sb0, sb1) (all of K unless split)
+  const int splits = (int)gridDim.z;
+  const int sb0 = splits > 1 ? (int)blockIdx.z * a.k_chunk : 0;
+  const int sb1 = splits > 1 ? min(a.nb, sb0 + a.k_chunk) : a.nb;
+  const int kb0 = sb0 * (256 / kPgBK);
+  const int nkb = (sb1 - sb0) * (256 / kPgBK);  // K steps
   if (threadIdx.x < BN / 2) {
     const int t = n_tile * (BN / 2) + threadIdx.x;
     xs_s[threadIdx.x] = t < a.n_tok ? a.xscale[t] : 0.0f;
@@ -234,7 +265,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         const int s = kb % kPgBStages;
         if (kb >= kPgBStages) mbar_wait(&b_empty[s], ((kb / kPgBStages) - 1) & 1);
         mbar_arrive_expect_tx(&b_full[s], (uint32_t)kPgBTile);
-        tma_load_2d(sb + s * kPgBTile, &xs_map, kb * kPgBK, n_tile * BN, &b_full[s]);
+        tma_load_2d(sb + s * kPgBTile, &xs_map, (kb0 + kb) * kPgBK, n_tile * BN, &b_full[s]);
       }
     }
   } else if (warp == 1) {
@@ -260,7 +291,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     // low-nibble half (k 0..31 of the step, warps 2-5) or the high-nibble half
     // (k 32..63, warps 6-9): two dequantizing warps per scheduler. Each
     // thread reads its row's 16-byte header and 128 quant bytes of a
-    // super-block column straight from global memory (L2: the 16 column tiles
+    // super-block column straight from global memory (L2: the column tiles
     // of this weight tile read the same bytes), one column ahead.
     const int i = threadIdx.x - 64;
     const int row = i & (kPgBM - 1), half = i >> 7;
@@ -280,16 +311,16 @@ __global__ void __launch_bounds__(kPgThreads, 1)
 #pragma unroll
       for (int j = 0; j < 8; ++j) nq[j] = row_live ? __ldg(qp + j) : z;
     };
-    fetch(0);
-    for (int sbk = 0; sbk < a.nb; ++sbk) {
+    fetch(sb0);
+    for (int sbk = sb0; sbk < sb1; ++sbk) {
       const uint4 hdr = nh;
       uint4 q[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) q[j] = nq[j];
-      if (sbk + 1 < a.nb) fetch(sbk + 1);
+      if (sbk + 1 < sb1) fetch(sbk + 1);
 #pragma unroll
       for (int chunk = 0; chunk < 4; ++chunk) {
-        const int kb = sbk * 4 + chunk, s = kb % kPgAStages;
+        const int kb = (sbk - sb0) * 4 + chunk, s = kb % kPgAStages;
         {
           const uint32_t k = 2u * (uint32_t)(chunk & 1);
           lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
@@ -333,15 +364,55 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     tc_fence_after();
     const int quad = warp & 3;
     const int m = m_tile * kPgBM + quad * 32 + lane;
-    const int cbeg = half * (BN / 2);
+    constexpr int kCols = BN / 2;                  // columns of this warp
+    const int cbeg = half * kCols;
     const bool row_ok = m < a.m_rows;
-    constexpr int CW = BN / 2 < 32 ? BN / 2 : 32;  // columns per TMEM read
+    constexpr int CW = kCols < 32 ? kCols : 32;    // columns per TMEM read
     constexpr int TPC = CW / 2;                    // tokens per TMEM read
-    for (int c0 = cbeg; c0 < cbeg + BN / 2; c0 += CW) {
+    const int prow = quad * 32 + lane;             // this lane's row of the tile
+    float* tile_part = nullptr;
+    if (splits > 1) {
+      // publish this split's partial tile; the last split to finish the
+      // tile runs the epilogue on the sum of all of them
+      tile_part = a.part + (size_t)(blockIdx.y * gridDim.x + n_tile) * splits * kPgBM * BN;
+      float* mine = tile_part + ((size_t)blockIdx.z * kPgBM + prow) * BN;
+      for (int c0 = cbeg; c0 < cbeg + kCols; c0 += CW) {
+        float v[CW];
+        tmem_ld_cols<CW>(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < CW; i += 4)
+          *reinterpret_cast<float4*>(mine + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const unsigned int ticket = atomicAdd(&a.tile_cnt[blockIdx.y * gridDim.x + n_tile], 1u);
+        *last_split = ticket == (unsigned int)splits - 1u;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+    }
+    const bool run_epi = splits == 1 || *last_split != 0;
+    if (run_epi && splits > 1) __threadfence();
+    for (int c0 = cbeg; run_epi && c0 < cbeg + kCols; c0 += CW) {
       float v[CW];
-      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
-      if constexpr (CW == 32) tmem_ld32(taddr, v);
-      else tmem_ld16(taddr, v);
+      if (splits == 1) {
+        tmem_ld_cols<CW>(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+      } else {
+        // the splits' partials summed in split order (deterministic)
+#pragma unroll
+        for (int i = 0; i < CW; ++i) v[i] = 0.0f;
+        for (int z = 0; z < splits; ++z) {
+          const float* pz = tile_part + ((size_t)z * kPgBM + prow) * BN + c0;
+#pragma unroll
+          for (int i = 0; i < CW; i += 4) {
+            const float4 f = __ldcg(reinterpret_cast<const float4*>(pz + i));
+            v[i] += f.x;
+            v[i + 1] += f.y;
+            v[i + 2] += f.z;
+            v[i + 3] += f.w;
+          }
+        }
+      }
       const int tb = (n_tile * BN + c0) / 2;  // first token of these column pairs
       float y[TPC];
 #pragma unroll
@@ -435,6 +506,8 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         }
       }
     }
+    // every split has taken its ticket: the counter is free for the next launch
+    if (splits > 1 && run_epi && threadIdx.x == 64) a.tile_cnt[blockIdx.y * gridDim.x + n_tile] = 0u;
     tc_fence_before();
   }
   __syncthreads();
