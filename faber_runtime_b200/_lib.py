@@ -94,6 +94,16 @@ SIGNATURES = {
     "faber_gpu_v2_session_last_greedy_ms": (Status, [P, ctypes.POINTER(ctypes.c_float)]),
     "faber_gpu_v2_session_commit": (Status, [P, I64, U32, U64, U64, ctypes.POINTER(I32)]),
     "faber_gpu_v2_nccl_unique_id": (Status, [P]),
+    "faber_gpu_v2_gguf_parse": (Status, [P, U64, PP]),
+    "faber_gpu_v2_gguf_info": (Status, [P, ctypes.POINTER(U32), ctypes.POINTER(U64), ctypes.POINTER(U64),
+                                        ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "faber_gpu_v2_gguf_tensor": (Status, [P, U64, P]),
+    "faber_gpu_v2_gguf_kv": (Status, [P, U64, ctypes.c_char_p, U64, ctypes.POINTER(U32), ctypes.POINTER(U32),
+                                      ctypes.POINTER(U64)]),
+    "faber_gpu_v2_gguf_get_int": (Status, [P, ctypes.c_char_p, ctypes.POINTER(I64)]),
+    "faber_gpu_v2_gguf_get_float": (Status, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    "faber_gpu_v2_gguf_get_string": (Status, [P, ctypes.c_char_p, ctypes.c_char_p, U64, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_gguf_free": (Status, [P]),
     "faber_gpu_v2_batch_open": (Status, [P, U32, PP]),
     "faber_gpu_v2_batch_greedy": (Status, [P, U32, P, U32, P, P]),
     "faber_gpu_v2_batch_last_ms": (Status, [P, ctypes.POINTER(ctypes.c_float)]),

@@ -14,6 +14,7 @@
 
 #include "abi.hpp"
 #include "gemv.cuh"
+#include "gguf.hpp"
 #include "ops.cuh"
 #include "repack.hpp"
 
@@ -570,6 +571,119 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_attention_de
     g_last_error = "faber_gpu_v2_attention_decode_static: unknown exception";
     return status(FABER_STATUS_PANIC);
   }
+}
+
+
+// ---- GGUF v3 reader ---------------------------------------------------------
+struct FaberGguf {
+  faber::GgufFile f;
+};
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_parse(const uint8_t* bytes,
+                                                                              uint64_t len,
+                                                                              FaberGguf** out) {
+  return guarded("faber_gpu_v2_gguf_parse", [&] {
+    FABER_ARG(out != nullptr && (bytes != nullptr || len == 0), "null pointer");
+    *out = nullptr;
+    auto g = std::make_unique<FaberGguf>();
+    g->f = gguf_parse(bytes, len);
+    *out = g.release();
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_info(
+    const FaberGguf* g, uint32_t* version, uint64_t* n_kv, uint64_t* n_tensors, uint64_t* data_offset,
+    uint64_t* alignment) {
+  return guarded("faber_gpu_v2_gguf_info", [&] {
+    FABER_ARG(g, "null reader");
+    if (version) *version = g->f.version;
+    if (n_kv) *n_kv = g->f.kv.size();
+    if (n_tensors) *n_tensors = g->f.tensors.size();
+    if (data_offset) *data_offset = g->f.data_offset;
+    if (alignment) *alignment = g->f.alignment;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_tensor(const FaberGguf* g,
+                                                                               uint64_t index,
+                                                                               FaberGgufTensorV1* out) {
+  return guarded("faber_gpu_v2_gguf_tensor", [&] {
+    FABER_ARG(g && out, "null pointer");
+    FABER_ARG(index < g->f.tensors.size(), "tensor index out of range");
+    const GgufTensor& t = g->f.tensors[index];
+    FABER_ARG(t.name.size() < sizeof(out->name), "tensor name longer than the descriptor holds");
+    std::memset(out, 0, sizeof(*out));
+    std::memcpy(out->name, t.name.data(), t.name.size());
+    out->ggml_type = t.type;
+    out->n_dims = t.n_dims;
+    for (uint32_t d = 0; d < 4; ++d) out->dims[d] = t.dims[d];
+    out->elements = t.elements;
+    out->nbytes = t.nbytes;
+    out->offset = t.offset;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_kv(
+    const FaberGguf* g, uint64_t index, char* key, uint64_t key_cap, uint32_t* type, uint32_t* arr_type,
+    uint64_t* arr_count) {
+  return guarded("faber_gpu_v2_gguf_kv", [&] {
+    FABER_ARG(g && key && key_cap > 0, "null pointer");
+    FABER_ARG(index < g->f.kv.size(), "KV index out of range");
+    const GgufKv& kv = g->f.kv[index];
+    require(kv.key.size() < key_cap, FABER_STATUS_IO_ERROR, "key buffer too small");
+    std::memcpy(key, kv.key.data(), kv.key.size());
+    key[kv.key.size()] = 0;
+    if (type) *type = kv.type;
+    if (arr_type) *arr_type = kv.arr_type;
+    if (arr_count) *arr_count = kv.arr_count;
+  });
+}
+
+// Scalar lookups by key: any integer type (and BOOL) as int64, F32/F64 as
+// double, STRING into buf. A missing key or another type is INVALID_ARGUMENT.
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_get_int(const FaberGguf* g,
+                                                                                const char* key,
+                                                                                int64_t* v) {
+  return guarded("faber_gpu_v2_gguf_get_int", [&] {
+    FABER_ARG(g && key && v, "null pointer");
+    const GgufKv* kv = g->f.find(key);
+    FABER_ARG(kv != nullptr, std::string("no metadata key ") + key);
+    FABER_ARG(kv->type != GGUF_STRING && kv->type != GGUF_ARRAY && kv->type != GGUF_F32 &&
+                  kv->type != GGUF_F64,
+              std::string(key) + " is not an integer");
+    FABER_ARG(kv->type != GGUF_U64 || kv->u <= (uint64_t)INT64_MAX, std::string(key) + " exceeds int64");
+    *v = kv->i;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_get_float(const FaberGguf* g,
+                                                                                  const char* key,
+                                                                                  double* v) {
+  return guarded("faber_gpu_v2_gguf_get_float", [&] {
+    FABER_ARG(g && key && v, "null pointer");
+    const GgufKv* kv = g->f.find(key);
+    FABER_ARG(kv != nullptr, std::string("no metadata key ") + key);
+    FABER_ARG(kv->type == GGUF_F32 || kv->type == GGUF_F64, std::string(key) + " is not a float");
+    *v = kv->f;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_get_string(
+    const FaberGguf* g, const char* key, char* buf, uint64_t cap, uint64_t* len) {
+  return guarded("faber_gpu_v2_gguf_get_string", [&] {
+    FABER_ARG(g && key && len, "null pointer");
+    const GgufKv* kv = g->f.find(key);
+    FABER_ARG(kv != nullptr, std::string("no metadata key ") + key);
+    FABER_ARG(kv->type == GGUF_STRING, std::string(key) + " is not a string");
+    *len = kv->s.size();
+    require(buf != nullptr && kv->s.size() < cap, FABER_STATUS_IO_ERROR, "string buffer too small");
+    std::memcpy(buf, kv->s.data(), kv->s.size());
+    buf[kv->s.size()] = 0;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_free(FaberGguf* g) {
+  return guarded("faber_gpu_v2_gguf_free", [&] { delete g; });
 }
 
 }  // extern "C"

@@ -56,6 +56,20 @@ enum {
 typedef struct FaberGpuModel FaberGpuModel;
 typedef struct FaberGpuSession FaberGpuSession;
 typedef struct FaberGpuBatch FaberGpuBatch;
+typedef struct FaberGguf FaberGguf;
+
+/* One tensor of a parsed GGUF file. dims are in GGML order (dims[0] is the
+ * contiguous one: a row's length); unused dims are 1. The data is
+ * bytes[offset, offset + nbytes) of the parsed buffer. */
+typedef struct FaberGgufTensorV1 {
+  char name[256];
+  uint32_t ggml_type;
+  uint32_t n_dims;
+  uint64_t dims[4];
+  uint64_t elements;
+  uint64_t nbytes;
+  uint64_t offset;
+} FaberGgufTensorV1;
 
 /* ------------------------------------------------------------------------
  * Library / diagnostics
@@ -234,6 +248,37 @@ FaberRtStatusV1 faber_gpu_v2_session_position_logits(FaberGpuSession* s, float* 
 FaberRtStatusV1 faber_gpu_v2_session_greedy(FaberGpuSession* s, uint32_t n_gen,
                                             const int64_t* eog, uint32_t n_eog,
                                             int64_t* out_tokens, int32_t* all_finite);
+/* GGUF v3 reader — the structural admission of src/gguf.rs:581-812 without
+ * its pin on one file (no SHA-256, size or count expectations):
+ *   - magic and version 3;
+ *   - counts bounded by the bytes left;
+ *   - length-capped UTF-8 keys, strings and names; unique keys and names;
+ *   - BOOL 0/1; no nested arrays;
+ *   - 1..4 dims, overflow-checked sizes;
+ *   - admitted dtypes F32, F16, Q5_0, Q8_0, Q4_K, Q6_K, in whole blocks;
+ *   - aligned, sequential, non-overlapping ranges inside the buffer.
+ * The first violation returns INVALID_ARGUMENT, and last_error names the
+ * reference's AdmissionError kind. The reader keeps offsets only; the
+ * caller keeps the bytes alive while it reads tensors. */
+FaberRtStatusV1 faber_gpu_v2_gguf_parse(const uint8_t* bytes, uint64_t len, FaberGguf** out);
+FaberRtStatusV1 faber_gpu_v2_gguf_info(const FaberGguf* g, uint32_t* version, uint64_t* n_kv,
+                                       uint64_t* n_tensors, uint64_t* data_offset,
+                                       uint64_t* alignment);
+FaberRtStatusV1 faber_gpu_v2_gguf_tensor(const FaberGguf* g, uint64_t index,
+                                         FaberGgufTensorV1* out);
+/* KV index -> key (NUL-terminated into key_cap bytes; IO_ERROR if short),
+ * value type, and for arrays the element type and count. */
+FaberRtStatusV1 faber_gpu_v2_gguf_kv(const FaberGguf* g, uint64_t index, char* key,
+                                     uint64_t key_cap, uint32_t* type, uint32_t* arr_type,
+                                     uint64_t* arr_count);
+/* Scalar metadata by key: any integer type or BOOL, F32/F64, STRING. A
+ * missing key or another type is INVALID_ARGUMENT. */
+FaberRtStatusV1 faber_gpu_v2_gguf_get_int(const FaberGguf* g, const char* key, int64_t* v);
+FaberRtStatusV1 faber_gpu_v2_gguf_get_float(const FaberGguf* g, const char* key, double* v);
+FaberRtStatusV1 faber_gpu_v2_gguf_get_string(const FaberGguf* g, const char* key, char* buf,
+                                             uint64_t cap, uint64_t* len);
+FaberRtStatusV1 faber_gpu_v2_gguf_free(FaberGguf* g);
+
 /* Batched greedy decode — run_greedy (src/greedy_run.rs:186-248) for up to
  * 16 sequences in lockstep, the batch-16 decode of the reference's
  * multi-sequence KvCacheLayout (src/kv_cache.rs:504-626, `slots`). The batch
