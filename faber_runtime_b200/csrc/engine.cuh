@@ -96,6 +96,8 @@ static const char* kLayerSlotNames[LS_N] = {"attn_norm", "attn_q", "attn_k", "at
 
 struct LayerDev {
   DeviceTiled qkv, o, gateup, down;
+  // the same linears as typed rows when a part is not Q4_K (valid() then)
+  DeviceRows qkv_r, o_r, gateup_r, down_r;
   DevBuf attn_norm, ffn_norm;
 };
 
@@ -112,6 +114,8 @@ struct ModelState {
   DevBuf embd_f16;   // [V][d] f16 (f16-rounded token_embd)
   DevBuf out_norm;   // [d] f32, not rounded
   DeviceTiled head;  // untied Q4_K head, local vocab rows
+  DeviceRows head_r; // ... as typed rows when it is not Q4_K
+  bool all_q4k = true;  // every linear in the Q4_K tile layout
   ncclComm_t comm = nullptr;
   int device = 0;
   uint64_t device_bytes = 0;
@@ -407,9 +411,24 @@ inline void model_set_tensor(ModelState& M, const std::string& name, uint32_t ty
       if (std::string(slot) == kLayerSlotNames[k]) h = &M.staged[layer][(size_t)k];
   }
   if (!sr.q4k) return f32_vec(*h, sr.rows);
+  if (type != FABER_GGML_Q4_K) {
+    // another admitted block type: kept whole, served by the row GEMV
+    int be = 0, bb = 0;
+    require(type != FABER_GGML_F32 && ggml_block_geometry(type, be, bb), FABER_STATUS_UNSUPPORTED,
+            name + ": linears must be Q4_K, Q6_K, Q5_0 or Q8_0");
+    require(M.tp == 1, FABER_STATUS_UNSUPPORTED,
+            name + ": only Q4_K linears shard across tensor-parallel ranks");
+    expect_shape(sr.rows, sr.cols);
+    FABER_ARG(sr.cols % (uint64_t)be == 0, name + ": rows are not whole blocks");
+    expect_bytes(sr.rows * sr.cols / be * bb);
+    h->type = type;
+    h->bytes.assign(src, src + nbytes);
+    h->rows = sr.rows;
+    h->cols = sr.cols;
+    h->set = true;
+    return;
+  }
   // Q4_K linear: this rank's block rows [r0, r0+nr) x cols [c0, c0+nc)
-  require(type == FABER_GGML_Q4_K, FABER_STATUS_UNSUPPORTED,
-          name + ": only Q4_K linears are supported on this path");
   expect_shape(sr.rows, sr.cols);
   FABER_ARG((sr.rows * sr.cols) % 256 == 0, name + ": element count not a multiple of 256");
   expect_bytes(sr.rows * sr.cols / 256 * kQ4kBlockBytes);
@@ -427,6 +446,37 @@ inline void model_set_tensor(ModelState& M, const std::string& name, uint32_t ty
 }
 
 inline uint64_t nblk(const HostTensor& h) { return h.rows * h.cols / 256; }
+
+// Typed rows of a fused linear: output row j is row part_row(j) of part(j).
+template <class PartOf>
+inline void rows_from(DeviceRows& D, int rows, int cols, PartOf part_of) {
+  const int n_tiles = (rows + kTileRows - 1) / kTileRows;
+  std::vector<uint64_t> off((size_t)n_tiles * kTileRows, 0);
+  std::vector<uint32_t> type((size_t)n_tiles * kTileRows, kNoRow);
+  uint64_t total = 0;
+  for (int j = 0; j < rows; ++j) {
+    const auto pr = part_of(j);
+    int be = 0, bb = 0;
+    ggml_block_geometry(pr.first->type, be, bb);
+    off[j] = total;
+    type[j] = pr.first->type;
+    total += (uint64_t)cols / be * bb;
+  }
+  std::vector<uint8_t> bytes(total);
+  for (int j = 0; j < rows; ++j) {
+    const auto pr = part_of(j);
+    int be = 0, bb = 0;
+    ggml_block_geometry(pr.first->type, be, bb);
+    const uint64_t rb = (uint64_t)cols / be * bb;
+    std::memcpy(bytes.data() + off[j], pr.first->bytes.data() + pr.second * rb, rb);
+  }
+  upload(D.bytes, bytes.data(), bytes.size());
+  upload(D.row_off, off.data(), off.size() * 8);
+  upload(D.row_type, type.data(), type.size() * 4);
+  D.n_tiles = n_tiles;
+  D.rows = rows;
+  D.cols = cols;
+}
 
 inline void model_finalize(ModelState& M) {
   const FaberModelConfigV1& c = M.cfg;
@@ -447,24 +497,51 @@ inline void model_finalize(ModelState& M) {
     auto& S = M.staged[l];
     LayerDev& L = M.layers[l];
     const uint64_t nq = (uint64_t)M.Hl * hd, nk = (uint64_t)M.Hkvl * hd;
+    auto q4k = [&](std::initializer_list<int> slots) {
+      for (int k : slots)
+        if (S[(size_t)k].type != FABER_GGML_Q4_K) return false;
+      return true;
+    };
     // fused QKV: rows [q | k | v]
-    L.qkv.from(repack_q4k((int)(nq + 2 * nk), (int)d, [&](int j) {
+    auto qkv_part = [&](int j) {
       const HostTensor& t = (uint64_t)j < nq ? S[LS_Q] : ((uint64_t)j < nq + nk ? S[LS_K] : S[LS_V]);
       const uint64_t r = (uint64_t)j < nq ? j : ((uint64_t)j < nq + nk ? j - nq : j - nq - nk);
-      return RowSeg{t.bytes.data(), nblk(t), r * d};
-    }));
-    L.o.from(repack_q4k((int)d, (int)S[LS_O].cols, [&](int j) {
-      return RowSeg{S[LS_O].bytes.data(), nblk(S[LS_O]), (uint64_t)j * S[LS_O].cols};
-    }));
+      return std::pair<const HostTensor*, uint64_t>(&t, r);
+    };
+    if (q4k({LS_Q, LS_K, LS_V}))
+      L.qkv.from(repack_q4k((int)(nq + 2 * nk), (int)d, [&](int j) {
+        const auto pr = qkv_part(j);
+        return RowSeg{pr.first->bytes.data(), nblk(*pr.first), pr.second * d};
+      }));
+    else
+      rows_from(L.qkv_r, (int)(nq + 2 * nk), (int)d, qkv_part);
+    auto o_part = [&](int j) { return std::pair<const HostTensor*, uint64_t>(&S[LS_O], (uint64_t)j); };
+    if (q4k({LS_O}))
+      L.o.from(repack_q4k((int)d, (int)S[LS_O].cols, [&](int j) {
+        return RowSeg{S[LS_O].bytes.data(), nblk(S[LS_O]), (uint64_t)j * S[LS_O].cols};
+      }));
+    else
+      rows_from(L.o_r, (int)d, (int)S[LS_O].cols, o_part);
     // gate/up interleaved: row 2f = gate f, 2f+1 = up f (SwiGLU epilogue pairs)
     const uint64_t Fl = S[LS_GATE].rows;
-    L.gateup.from(repack_q4k((int)(2 * Fl), (int)d, [&](int j) {
-      const HostTensor& t = (j & 1) ? S[LS_UP] : S[LS_GATE];
-      return RowSeg{t.bytes.data(), nblk(t), (uint64_t)(j >> 1) * d};
-    }));
-    L.down.from(repack_q4k((int)d, (int)S[LS_DOWN].cols, [&](int j) {
-      return RowSeg{S[LS_DOWN].bytes.data(), nblk(S[LS_DOWN]), (uint64_t)j * S[LS_DOWN].cols};
-    }));
+    auto gu_part = [&](int j) {
+      return std::pair<const HostTensor*, uint64_t>((j & 1) ? &S[LS_UP] : &S[LS_GATE], (uint64_t)(j >> 1));
+    };
+    if (q4k({LS_GATE, LS_UP}))
+      L.gateup.from(repack_q4k((int)(2 * Fl), (int)d, [&](int j) {
+        const auto pr = gu_part(j);
+        return RowSeg{pr.first->bytes.data(), nblk(*pr.first), pr.second * d};
+      }));
+    else
+      rows_from(L.gateup_r, (int)(2 * Fl), (int)d, gu_part);
+    auto down_part = [&](int j) { return std::pair<const HostTensor*, uint64_t>(&S[LS_DOWN], (uint64_t)j); };
+    if (q4k({LS_DOWN}))
+      L.down.from(repack_q4k((int)d, (int)S[LS_DOWN].cols, [&](int j) {
+        return RowSeg{S[LS_DOWN].bytes.data(), nblk(S[LS_DOWN]), (uint64_t)j * S[LS_DOWN].cols};
+      }));
+    else
+      rows_from(L.down_r, (int)d, (int)S[LS_DOWN].cols, down_part);
+    if (L.qkv_r.valid() || L.o_r.valid() || L.gateup_r.valid() || L.down_r.valid()) M.all_q4k = false;
     // per-layer norms are f16-rounded like every per-layer tensor
     // (src/cpu_oracle.rs:323-331)
     for (int k : {LS_ATTN_NORM, LS_FFN_NORM}) {
@@ -474,6 +551,7 @@ inline void model_finalize(ModelState& M) {
       upload(k == LS_ATTN_NORM ? L.attn_norm : L.ffn_norm, w.data(), d * 4);
     }
     bytes += L.qkv.w.n + L.o.w.n + L.gateup.w.n + L.down.w.n + 2 * d * 4;
+    bytes += L.qkv_r.bytes.n + L.o_r.bytes.n + L.gateup_r.bytes.n + L.down_r.bytes.n;
     for (auto& t : S) {
       std::vector<uint8_t>().swap(t.bytes);
     }
@@ -489,7 +567,14 @@ inline void model_finalize(ModelState& M) {
     std::vector<uint8_t>().swap(M.st_embd.bytes);
   }
   upload(M.out_norm, M.st_out_norm.bytes.data(), d * 4);  // not rounded (src/cpu_oracle.rs:434)
-  if (!c.tied_head) {
+  if (!c.tied_head && M.st_output.type != FABER_GGML_Q4_K) {
+    rows_from(M.head_r, (int)M.st_output.rows, (int)d, [&](int j) {
+      return std::pair<const HostTensor*, uint64_t>(&M.st_output, (uint64_t)j);
+    });
+    M.all_q4k = false;
+    bytes += M.head_r.bytes.n;
+    std::vector<uint8_t>().swap(M.st_output.bytes);
+  } else if (!c.tied_head) {
     M.head.from(repack_q4k((int)M.st_output.rows, (int)d, [&](int j) {
       return RowSeg{M.st_output.bytes.data(), nblk(M.st_output), (uint64_t)j * d};
     }));
@@ -637,7 +722,7 @@ inline void enqueue_push(SessionState& S, bool pdl) {
     float* tr = S.trace ? S.tr.as<float>() + (size_t)l * 8 * S.tr_w : nullptr;
     // QKV
     {
-      GemvArgs a = L.qkv.args();
+      GemvArgs a = L.qkv_r.valid() ? L.qkv_r.gemv_args() : L.qkv.args();
       a.norm_w = L.attn_norm.as<float>();
       a.eps = c.rms_eps;
       a.q_out = S.q.as<float>();
@@ -661,7 +746,8 @@ inline void enqueue_push(SessionState& S, bool pdl) {
         launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_QKV>(a, S.stream, pdl);
       } else {
         a.x = S.h.as<float>();
-        launch_gemv<WL_TILED, PRO_NORM, EPI_QKV>(a, S.stream, pdl);
+        if (L.qkv_r.valid()) launch_gemv_rows<PRO_NORM, EPI_QKV>(a, L.qkv_r, S.stream, pdl);
+        else launch_gemv<WL_TILED, PRO_NORM, EPI_QKV>(a, S.stream, pdl);
       }
       if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 1 * S.tr_w, S.q.p, nq * 4, cudaMemcpyDeviceToDevice, S.stream));
     }
@@ -689,7 +775,7 @@ inline void enqueue_push(SessionState& S, bool pdl) {
     }
     // O projection (+ residual)
     {
-      GemvArgs a = L.o.args();
+      GemvArgs a = L.o_r.valid() ? L.o_r.gemv_args() : L.o.args();
       a.x = S.ctx.as<float>();
       if (M.tp > 1) {
         tp_publish_args(S, a, 0, l);
@@ -697,12 +783,13 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       } else {
         a.out = S.h2.as<float>();
         a.res = S.h.as<float>();
-        launch_gemv<WL_TILED, PRO_PLAIN, EPI_RESID>(a, S.stream, pdl);
+        if (L.o_r.valid()) launch_gemv_rows<PRO_PLAIN, EPI_RESID>(a, L.o_r, S.stream, pdl);
+        else launch_gemv<WL_TILED, PRO_PLAIN, EPI_RESID>(a, S.stream, pdl);
       }
     }
     // gate/up + SwiGLU
     {
-      GemvArgs a = L.gateup.args();
+      GemvArgs a = L.gateup_r.valid() ? L.gateup_r.gemv_args() : L.gateup.args();
       a.norm_w = L.ffn_norm.as<float>();
       a.eps = c.rms_eps;
       a.out = S.hh.as<float>();
@@ -714,7 +801,8 @@ inline void enqueue_push(SessionState& S, bool pdl) {
         launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_SWIGLU>(a, S.stream, pdl);
       } else {
         a.x = S.h2.as<float>();
-        launch_gemv<WL_TILED, PRO_NORM, EPI_SWIGLU>(a, S.stream, pdl);
+        if (L.gateup_r.valid()) launch_gemv_rows<PRO_NORM, EPI_SWIGLU>(a, L.gateup_r, S.stream, pdl);
+        else launch_gemv<WL_TILED, PRO_NORM, EPI_SWIGLU>(a, S.stream, pdl);
       }
       if (tr) {
         FABER_CUDA(cudaMemcpyAsync(tr + 5 * S.tr_w, S.h2.p, (size_t)d * 4, cudaMemcpyDeviceToDevice, S.stream));
@@ -723,7 +811,7 @@ inline void enqueue_push(SessionState& S, bool pdl) {
     }
     // down (+ residual)
     {
-      GemvArgs a = L.down.args();
+      GemvArgs a = L.down_r.valid() ? L.down_r.gemv_args() : L.down.args();
       a.x = S.hh.as<float>();
       if (M.tp > 1) {
         tp_publish_args(S, a, 1, l);
@@ -731,7 +819,8 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       } else {
         a.out = S.h.as<float>();
         a.res = S.h2.as<float>();
-        launch_gemv<WL_TILED, PRO_PLAIN, EPI_RESID>(a, S.stream, pdl);
+        if (L.down_r.valid()) launch_gemv_rows<PRO_PLAIN, EPI_RESID>(a, L.down_r, S.stream, pdl);
+        else launch_gemv<WL_TILED, PRO_PLAIN, EPI_RESID>(a, S.stream, pdl);
         if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 7 * S.tr_w, S.h.p, (size_t)d * 4, cudaMemcpyDeviceToDevice, S.stream));
       }
     }
@@ -751,7 +840,7 @@ inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>
     a.nb = (int)c.d_model / 256;
     a.n_tiles = (M.Vl + kTileRows - 1) / kTileRows;
   } else {
-    a = M.head.args();
+    a = M.head_r.valid() ? M.head_r.gemv_args() : M.head.args();
   }
   a.norm_w = M.out_norm.as<float>();
   a.eps = c.rms_eps;
@@ -773,6 +862,8 @@ inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>
   if (c.tied_head) {
     if (res) launch_gemv<WL_F16, PRO_NORM_PEERS, EPI_LOGITS>(a, S.stream, pdl);
     else launch_gemv<WL_F16, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
+  } else if (M.head_r.valid()) {
+    launch_gemv_rows<PRO_NORM, EPI_LOGITS>(a, M.head_r, S.stream, pdl);
   } else {
     if (res) launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_LOGITS>(a, S.stream, pdl);
     else launch_gemv<WL_TILED, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
@@ -849,7 +940,7 @@ constexpr uint64_t kPrefillMinTokens = 32;
 inline bool prefill_supported(const ModelState& M) {
   const FaberModelConfigV1& c = M.cfg;
   const uint32_t nq = (uint32_t)M.Hl * c.head_dim;
-  return M.tp == 1 && c.d_model % 256 == 0 && nq % 256 == 0 && M.Fl % 256 == 0;
+  return M.tp == 1 && M.all_q4k && c.d_model % 256 == 0 && nq % 256 == 0 && M.Fl % 256 == 0;
 }
 
 using TmapEncode = PFN_cuTensorMapEncodeTiled_v12000;

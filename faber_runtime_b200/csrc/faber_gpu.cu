@@ -14,6 +14,7 @@
 
 #include "abi.hpp"
 #include "gemv.cuh"
+#include "gemv_rows.cuh"
 #include "gguf.hpp"
 #include "ops.cuh"
 #include "repack.hpp"
@@ -216,6 +217,56 @@ struct DeviceTiled {
   }
 };
 
+// A linear stored as rows of native GGML blocks (any admitted type per row),
+// in the fused order of the epilogues, padded to whole 16-row tiles.
+struct DeviceRows {
+  DevBuf bytes, row_off, row_type;
+  int n_tiles = 0, rows = 0, cols = 0;
+  bool valid() const { return rows > 0; }
+  RowsArgs args() const {
+    RowsArgs r;
+    r.bytes = bytes.as<uint8_t>();
+    r.row_off = row_off.as<uint64_t>();
+    r.row_type = row_type.as<uint32_t>();
+    r.n_tiles = n_tiles;
+    r.cols = cols;
+    return r;
+  }
+  GemvArgs gemv_args() const {
+    GemvArgs a = {};
+    a.n_tiles = n_tiles;
+    a.n_rows = rows;
+    a.n_cols = cols;
+    return a;
+  }
+};
+
+template <int PRO, int EPI>
+void launch_gemv_rows(const GemvArgs& a, const DeviceRows& W, cudaStream_t stream, bool pdl) {
+  auto kern = gemv_rows_kernel<PRO, EPI>;
+  static thread_local std::map<int, bool> attr_done;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_done[dev] = true;
+  }
+  const size_t smem = (size_t)W.cols * 4;
+  require(smem <= 200 * 1024, FABER_STATUS_UNSUPPORTED, "input too long for the row GEMV's staging");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::max(1, std::min(W.n_tiles, 4 * device_info().sms)));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  FABER_CUDA(cudaLaunchKernelEx(&cfg, kern, a, W.args()));
+}
+
+
 }  // namespace faber
 
 struct FaberGpuQ4kTensor {
@@ -325,6 +376,21 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_dequant_q4k(
     const uint64_t threads = n_blocks * 32;
     dequant_q4k_native_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
         blocks, n_blocks, out, f16_round ? 1 : 0);
+    FABER_CUDA(cudaGetLastError());
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_dequant_blocks(
+    uint32_t ggml_type, const uint8_t* blocks, uint64_t n_blocks, float* out, int32_t f16_round,
+    void* stream) {
+  return guarded("faber_gpu_v2_dequant_blocks", [&] {
+    int be = 0, bb = 0;
+    FABER_ARG(ggml_block_geometry(ggml_type, be, bb), "unknown GGML type " + std::to_string(ggml_type));
+    FABER_ARG(n_blocks == 0 || (blocks && out), "null pointer");
+    if (n_blocks == 0) return;
+    const uint64_t threads = n_blocks * 32;
+    dequant_blocks_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+        ggml_type, blocks, n_blocks, out, f16_round ? 1 : 0);
     FABER_CUDA(cudaGetLastError());
   });
 }

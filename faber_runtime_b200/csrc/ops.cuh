@@ -38,6 +38,92 @@ __device__ __forceinline__ float q4k_value(const uint8_t* blk, int e) {
   return __fsub_rn(__fmul_rn(d1, (float)q), m1);
 }
 
+// ---------------------------------------------------------------------------
+// The other admitted block types, bit-exact (src/dequant.rs:151-174,224-255):
+// element e of one block, every product rounded as the reference writes it.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kGgmlF32 = 0, kGgmlF16 = 1, kGgmlQ5_0 = 6, kGgmlQ8_0 = 8, kGgmlQ4_K = 12,
+                   kGgmlQ6_K = 14;
+
+__device__ __forceinline__ float blk_half(const uint8_t* p) {
+  return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+// dequant_q8_0 (src/dequant.rs:151-154): (i8) q * d, 32 per 34-byte block.
+__device__ __forceinline__ float q8_0_value(const uint8_t* blk, int e) {
+  return __fmul_rn((float)(int8_t)blk[2 + e], blk_half(blk));
+}
+
+// dequant_q5_0 (src/dequant.rs:160-174): 4 low bits in qs, the fifth from qh;
+// elements j and j + 16 share byte qs[j].
+__device__ __forceinline__ float q5_0_value(const uint8_t* blk, int e) {
+  const uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) |
+                      ((uint32_t)blk[5] << 24);
+  const int j = e & 15;
+  const uint8_t q = blk[6 + j];
+  const int x = e < 16 ? (int)((q & 0x0fu) | (((qh >> j) << 4) & 0x10u)) - 16
+                       : (int)((q >> 4) | ((qh >> (j + 12)) & 0x10u)) - 16;
+  return __fmul_rn((float)x, blk_half(blk));
+}
+
+// dequant_q6_k (src/dequant.rs:224-255): (d * sc) * q, 256 per 210-byte
+// block (ql 128 B, qh 64 B, 16 signed scales, d at byte 208).
+__device__ __forceinline__ float q6_k_value(const uint8_t* blk, int e) {
+  const int n = e & 128, r = e & 127;
+  const int g = r >> 5, l = r & 31;  // quarter of the 128-half, position
+  const uint8_t* ql = blk + (n >> 1);
+  const uint8_t qhb = blk[128 + (n >> 2) + l];
+  const uint8_t lo = (g & 1) ? ql[l + 32] : ql[l];
+  const int q = (int)(((g & 2) ? (lo >> 4) : (lo & 0x0f)) | (((qhb >> (2 * g)) & 3) << 4)) - 32;
+  const float sc = (float)(int8_t)blk[192 + (n >> 4) + (l >> 4) + 2 * g];
+  return __fmul_rn(__fmul_rn(blk_half(blk + 208), sc), (float)q);
+}
+
+__host__ __device__ inline bool ggml_block_geometry(uint32_t t, int& elems, int& bytes) {
+  switch (t) {
+    case kGgmlF32: elems = 1; bytes = 4; return true;
+    case kGgmlF16: elems = 1; bytes = 2; return true;
+    case kGgmlQ5_0: elems = 32; bytes = 22; return true;
+    case kGgmlQ8_0: elems = 32; bytes = 34; return true;
+    case kGgmlQ4_K: elems = 256; bytes = 144; return true;
+    case kGgmlQ6_K: elems = 256; bytes = 210; return true;
+    default: return false;
+  }
+}
+
+// Element e of one block of type t (any admitted type).
+__device__ __forceinline__ float block_value(uint32_t t, const uint8_t* blk, int e) {
+  switch (t) {
+    case kGgmlQ4_K: return q4k_value(blk, e);
+    case kGgmlQ6_K: return q6_k_value(blk, e);
+    case kGgmlQ8_0: return q8_0_value(blk, e);
+    case kGgmlQ5_0: return q5_0_value(blk, e);
+    case kGgmlF16: return blk_half(blk);
+    default: {
+      float v;
+      memcpy(&v, blk, 4);
+      return v;
+    }
+  }
+}
+
+// Validation surface for every block type: a block per warp, lanes stride its
+// elements.
+__global__ void dequant_blocks_kernel(uint32_t type, const uint8_t* __restrict__ blocks,
+                                      uint64_t n_blocks, float* __restrict__ out, int f16r) {
+  int be = 0, bb = 0;
+  ggml_block_geometry(type, be, bb);
+  const uint64_t wid = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= n_blocks) return;
+  const uint8_t* blk = blocks + wid * bb;
+  for (int e = lane; e < be; e += 32) {
+    float v = block_value(type, blk, e);
+    if (f16r) v = f16_round(v);
+    out[wid * be + e] = v;
+  }
+}
+
 // One warp per block, lanes stride the 256 elements (coalesced stores).
 __global__ void dequant_q4k_native_kernel(const uint8_t* __restrict__ blocks, uint64_t n_blocks,
                                           float* __restrict__ out, int f16r) {

@@ -25,6 +25,13 @@ def dequant_q4k(blocks_ptr: int, n_blocks: int, out_ptr: int, f16_round: bool = 
     _lib.call("faber_gpu_v2_dequant_q4k", blocks_ptr, n_blocks, out_ptr, int(f16_round), stream)
 
 
+def dequant_blocks(ggml_type: int, blocks_ptr: int, n_blocks: int, out_ptr: int,
+                   f16_round: bool = False, stream: int = 0) -> None:
+    """Any admitted block type (Q4_K, Q6_K, Q5_0, Q8_0, F32, F16) to f32."""
+    _lib.call("faber_gpu_v2_dequant_blocks", ggml_type, blocks_ptr, n_blocks, out_ptr, int(f16_round),
+              stream)
+
+
 def f16_round(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
     _lib.call("faber_gpu_v2_f16_round", x_ptr, y_ptr, n, stream)
 

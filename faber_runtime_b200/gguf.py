@@ -4,10 +4,11 @@ a loader that builds a DeviceModel from a llama-architecture file.
 The reference admits one pinned file (src/gguf.rs:581-812); the reader here
 keeps its structural checks without the pin. The loader maps the llama.*
 metadata to a ModelConfig and uploads every tensor as its raw GGUF blocks
-(the same bytes src/gguf.rs hands to CpuOracle::build). The decoder's GEMV
-takes Q4_K linears; a file whose linears use another type is refused with
-UNSUPPORTED. The embedding may be F32, F16 (widened exactly) or Q4_K
-(dequantized on the GPU; the model then rounds it to f16 like the
+(the same bytes src/gguf.rs hands to CpuOracle::build). Linears may be
+Q4_K (the tiled tensor-core GEMV) or Q6_K, Q5_0 and Q8_0 (the typed-row
+GEMV; a Q4_K_M file mixes them); others are refused with UNSUPPORTED. The
+embedding may be F32, F16 (widened exactly) or any of those block types
+(dequantized exactly on the GPU; the model then rounds it to f16 like the
 reference's token_embd).
 """
 
@@ -157,13 +158,15 @@ def _embedding_f32(g: GgufFile, t: TensorInfo, device: int) -> np.ndarray:
         return raw.view(np.float32)
     if t.ggml_type == GGML_F16:
         return raw.view(np.float16).astype(np.float32)
-    if t.ggml_type == GGML_Q4_K:
+    if t.ggml_type in (GGML_Q4_K, GGML_Q6_K, GGML_Q5_0, GGML_Q8_0):
         import torch
         from . import dequant
+        be = 256 if t.ggml_type in (GGML_Q4_K, GGML_Q6_K) else 32
         blocks = torch.from_numpy(np.ascontiguousarray(raw)).to(f"cuda:{device}")
         out = torch.empty(t.elements, dtype=torch.float32, device=f"cuda:{device}")
-        dequant.dequant_q4k(blocks.data_ptr(), t.elements // 256, out.data_ptr(), f16_round=False,
-                            stream=torch.cuda.current_stream(device).cuda_stream)
+        dequant.dequant_blocks(t.ggml_type, blocks.data_ptr(), t.elements // be, out.data_ptr(),
+                               f16_round=False, stream=torch.cuda.current_stream(device).cuda_stream)
+        torch.cuda.synchronize(device)
         return out.cpu().numpy()
     raise _lib.FaberError(4, f"{t.name}: a {GGML_NAMES[t.ggml_type]} embedding is not supported")
 
@@ -178,10 +181,10 @@ def model_tensors(g: GgufFile, cfg: ModelConfig, device: int = 0):
                 raise _lib.FaberError(4, f"{t.name}: norms must be F32")
             yield t.name, GGML_F32, g.tensor_bytes(t.name).view(np.float32), t.rows, 1
         else:
-            if t.ggml_type != GGML_Q4_K:
+            if t.ggml_type not in (GGML_Q4_K, GGML_Q6_K, GGML_Q5_0, GGML_Q8_0):
                 raise _lib.FaberError(4, f"{t.name}: {GGML_NAMES[t.ggml_type]} linears are not supported "
-                                         "(the decoder's GEMV takes Q4_K)")
-            yield t.name, GGML_Q4_K, g.tensor_bytes(t.name), t.rows, t.cols
+                                         "(the decoder takes Q4_K, Q6_K, Q5_0 and Q8_0)")
+            yield t.name, t.ggml_type, g.tensor_bytes(t.name), t.rows, t.cols
 
 
 def load_llama(path, device: int = 0, tp_size: int = 1, tp_rank: int = 0, nccl_uid: bytes = b""):

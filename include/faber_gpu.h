@@ -119,6 +119,12 @@ FaberRtStatusV1 faber_gpu_v2_buffer_device_ptr(uint64_t logical_id, void** dev_p
  * Bit-exact with the reference. */
 FaberRtStatusV1 faber_gpu_v2_dequant_q4k(const uint8_t* blocks, uint64_t n_blocks, float* out,
                                          int32_t f16_round, void* stream);
+/* Every admitted block type (dequant_q8_0 / dequant_q5_0 / dequant_q4_k /
+ * dequant_q6_k, src/dequant.rs:151-255, and F32/F16), bit-exact: n_blocks
+ * blocks of ggml_type on the device -> f32 (f16-rounded if f16_round). */
+FaberRtStatusV1 faber_gpu_v2_dequant_blocks(uint32_t ggml_type, const uint8_t* blocks,
+                                            uint64_t n_blocks, float* out, int32_t f16_round,
+                                            void* stream);
 
 /* f32 -> f16 (round-to-nearest-even) -> f32, element-wise: kv_f16_round
  * (src/cpu_oracle.rs:225-294). */

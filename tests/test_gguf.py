@@ -194,14 +194,14 @@ def test_loader_refuses_unsupported_files(faber):
     with pytest.raises(FaberError) as e:
         gguf.llama_config(gguf.GgufFile(write_gguf(kvs2, bad)))
     assert e.value.code == 4 and "ArchitectureMismatch" in str(e.value)
-    # a Q8_0 linear parses, but the decoder takes Q4_K
+    # an F16 linear parses, but the decoder takes Q4_K, Q6_K, Q5_0 and Q8_0
     i = [n for n, *_ in tensors].index("blk.0.attn_q.weight")
     n, _, d, _ = tensors[i]
-    q8 = tensors[:i] + [(n, 8, d, bytes(d[0] * d[1] // 32 * 34))] + tensors[i + 1:]
-    g = gguf.GgufFile(write_gguf(kvs, q8))
+    f16 = tensors[:i] + [(n, 1, d, bytes(d[0] * d[1] * 2))] + tensors[i + 1:]
+    g = gguf.GgufFile(write_gguf(kvs, f16))
     with pytest.raises(FaberError) as e:
         list(gguf.model_tensors(g, gguf.llama_config(g)))
-    assert e.value.code == 4 and "Q8_0" in str(e.value)
+    assert e.value.code == 4 and "F16" in str(e.value)
 
 
 @pytest.mark.gpu
@@ -221,3 +221,69 @@ def test_loaded_gguf_decodes_like_the_oracle(cuda, tmp_path):
     run.close()
     model.close()
     g.close()
+
+
+def typed_blocks(rng, gtype, n_blocks):
+    """Random blocks of Q8_0 / Q5_0 / Q6_K with scales that keep the
+    weights near the synthetic Q4_K ones in size."""
+    from faber_runtime_b200 import gguf
+    bb = {gguf.GGML_Q8_0: 34, gguf.GGML_Q5_0: 22, gguf.GGML_Q6_K: 210}[gtype]
+    b = rng.integers(0, 256, (n_blocks, bb), dtype=np.uint8)
+    lo, hi, at = {gguf.GGML_Q8_0: (2e-3, 1e-2, 0), gguf.GGML_Q5_0: (1e-2, 5e-2, 0),
+                  gguf.GGML_Q6_K: (2e-4, 1e-3, 208)}[gtype]
+    d = rng.uniform(lo, hi, n_blocks).astype(np.float16)
+    b[:, at:at + 2] = d.view(np.uint8).reshape(n_blocks, 2)
+    return b.reshape(-1)
+
+
+@pytest.mark.gpu
+def test_mixed_type_gguf_decodes_like_the_oracle(cuda, tmp_path):
+    """A Q4_K_M-like file: attn_k Q5_0, attn_v Q6_K, ffn_down Q8_0 and the head
+    Q6_K in every layer; the rest Q4_K. The typed-row GEMV serves the mixed
+    linears; tokens equal the oracle's and logits stay within 1e-3 x RMS."""
+    import oracle as o
+    from faber_runtime_b200 import ForwardRun, ModelConfig, gguf, synth
+    cfg = ModelConfig(n_layers=2, d_model=512, n_heads=8, n_kv_heads=4, head_dim=64, ffn=1536,
+                      vocab=4096, tied_head=False, rope_theta=10000.0, name="mixed")
+    rng = np.random.default_rng(17)
+    swap = {"blk.{}.attn_k": gguf.GGML_Q5_0, "blk.{}.attn_v": gguf.GGML_Q6_K,
+            "blk.{}.ffn_down": gguf.GGML_Q8_0}
+    tensors, oracle_t = [], {}
+    for name, ty, arr, rows, cols in synth.model_tensors(cfg, 17, norms="random"):
+        layer_key = name.replace(name.split(".")[1], "{}") if name.startswith("blk.") else name
+        nt = swap.get(layer_key, gguf.GGML_Q6_K if name == "output" else None)
+        if nt is not None:
+            be = 32 if nt in (gguf.GGML_Q8_0, gguf.GGML_Q5_0) else 256
+            ty, arr = nt, typed_blocks(rng, nt, rows * cols // be)
+        oracle_t[name] = (ty, arr, rows, cols)
+        dims = [rows] if cols == 1 else [cols, rows]
+        tensors.append((name + ".weight", ty, dims, np.ascontiguousarray(arr).tobytes()))
+    _, kvs, _ = llama_file()
+    kvs = [(k, t, v) for k, t, v in kvs]
+    p = tmp_path / "mixed.gguf"
+    p.write_bytes(write_gguf(kvs_for(cfg, kvs), tensors))
+    model, g = gguf.load_llama(p)
+    om = o.OracleModel(cfg, oracle_t)
+    prompt = synth.tokens(17, 2, 40, cfg.vocab)  # pushed token by token (typed rows)
+    ref, ref_logits, _ = om.greedy(prompt, 8, want_logits=True)
+    run = ForwardRun(model, prompt, context_length=64)
+    for i in range(8):
+        got = run.position_logits()
+        rms = np.sqrt(np.mean(np.asarray(ref_logits[i], np.float64) ** 2))
+        assert np.max(np.abs(got - ref_logits[i])) <= 1e-3 * rms
+        run.push_token(int(ref[i]))
+    run2 = ForwardRun(model, prompt, context_length=64)
+    toks, fin = run2.greedy(8)
+    assert fin and toks.tolist() == ref.tolist()
+    run.close()
+    run2.close()
+    model.close()
+    g.close()
+
+
+def kvs_for(cfg, kvs):
+    """The test file's llama metadata rewritten for cfg."""
+    vals = {"llama.block_count": cfg.n_layers, "llama.embedding_length": cfg.d_model,
+            "llama.attention.head_count": cfg.n_heads, "llama.attention.head_count_kv": cfg.n_kv_heads,
+            "llama.feed_forward_length": cfg.ffn}
+    return [(k, t, vals.get(k, v)) for k, t, v in kvs]

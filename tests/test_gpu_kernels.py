@@ -217,3 +217,29 @@ def test_placement_abi_round_trip(cuda):
     dequant.copy_in(42, b"")  # replaces with an empty buffer
     assert dequant.readback(42, 10) == b""
     dequant.sync(42)
+
+
+@pytest.mark.parametrize("gtype", [6, 8, 14])  # Q5_0, Q8_0, Q6_K
+def test_dequant_other_block_types_bit_exact(cuda, oracle, gtype):
+    """dequant_q5_0 / dequant_q8_0 / dequant_q6_k (src/dequant.rs:151-255)
+    on the GPU equal the oracle's to the bit, raw and f16-rounded, over random
+    blocks whose f16 scale runs through the special values."""
+    from faber_runtime_b200 import dequant
+    bb, be, at = {6: (22, 32, 0), 8: (34, 32, 0), 14: (210, 256, 208)}[gtype]
+    rng = np.random.default_rng(gtype)
+    n = 4096
+    blocks = rng.integers(0, 256, (n, bb), dtype=np.uint8)
+    specials = [0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x3C00, 0xBC00, 0x3555, 0x1000, 0x5000, 0x7BFF]
+    for i in range(n):
+        v = specials[i % len(specials)] if i < 8 * len(specials) else int(rng.integers(0x1000, 0x2400))
+        blocks[i, at:at + 2] = np.frombuffer(np.uint16(v).tobytes(), np.uint8)
+    blocks = blocks.reshape(-1)
+    d = to_dev(blocks)
+    out = torch.empty(n * be, dtype=torch.float32, device=cuda)
+    ref = oracle.dequant_row(gtype, blocks)
+    dequant.dequant_blocks(gtype, d.data_ptr(), n, out.data_ptr(), f16_round=False)
+    torch.cuda.synchronize()
+    same_bits(out.cpu().numpy(), ref)
+    dequant.dequant_blocks(gtype, d.data_ptr(), n, out.data_ptr(), f16_round=True)
+    torch.cuda.synchronize()
+    same_bits(out.cpu().numpy(), oracle.f16_round(ref))
