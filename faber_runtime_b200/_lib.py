@@ -66,6 +66,9 @@ SIGNATURES = {
     "faber_gpu_v2_buffer_device_ptr": (Status, [U64, PP, ctypes.POINTER(U64)]),
     "faber_gpu_v2_dequant_q4k": (Status, [P, U64, P, I32, P]),
     "faber_gpu_v2_dequant_blocks": (Status, [U32, P, U64, P, I32, P]),
+    "faber_gpu_v2_typed_upload": (Status, [U32, P, U64, U64, U64, PP]),
+    "faber_gpu_v2_typed_gemv": (Status, [P, P, P, P]),
+    "faber_gpu_v2_typed_free": (Status, [P]),
     "faber_gpu_v2_f16_round": (Status, [P, P, U64, P]),
     "faber_gpu_v2_gemv_q4k": (Status, [P, U64, U64, P, P, P]),
     "faber_gpu_v2_q4k_upload": (Status, [P, U64, U64, U64, PP]),

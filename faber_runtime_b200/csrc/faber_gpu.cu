@@ -447,6 +447,51 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_upload(
   });
 }
 
+// A linear of any admitted block type, as typed rows (validation surface of
+// the row GEMV the decoder uses for non-Q4_K linears).
+struct FaberGpuTypedTensor {
+  faber::DeviceRows r;
+};
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_typed_upload(
+    uint32_t ggml_type, const uint8_t* host_blocks, uint64_t nbytes, uint64_t rows, uint64_t cols,
+    FaberGpuTypedTensor** out) {
+  return guarded("faber_gpu_v2_typed_upload", [&] {
+    FABER_ARG(out != nullptr && host_blocks != nullptr, "null pointer");
+    *out = nullptr;
+    int be = 0, bb = 0;
+    FABER_ARG(ggml_block_geometry(ggml_type, be, bb), "unknown GGML type " + std::to_string(ggml_type));
+    FABER_ARG(rows > 0 && cols > 0 && cols % (uint64_t)be == 0, "rows must be whole blocks");
+    FABER_ARG(nbytes == rows * cols / be * bb, "packed tensor is " + std::to_string(nbytes) +
+                                                   " bytes, expected exactly " +
+                                                   std::to_string(rows * cols / be * bb));
+    HostTensor h;
+    h.type = ggml_type;
+    h.rows = rows;
+    h.cols = cols;
+    h.bytes.assign(host_blocks, host_blocks + nbytes);
+    auto t = std::make_unique<FaberGpuTypedTensor>();
+    rows_from(t->r, (int)rows, (int)cols,
+              [&](int j) { return std::pair<const HostTensor*, uint64_t>(&h, (uint64_t)j); });
+    *out = t.release();
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_typed_gemv(
+    const FaberGpuTypedTensor* t, const float* x, float* y, void* stream) {
+  return guarded("faber_gpu_v2_typed_gemv", [&] {
+    FABER_ARG(t && x && y, "null pointer");
+    GemvArgs a = t->r.gemv_args();
+    a.x = x;
+    a.out = y;
+    launch_gemv_rows<PRO_PLAIN, EPI_STORE>(a, t->r, as_stream(stream), false);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_typed_free(FaberGpuTypedTensor* t) {
+  return guarded("faber_gpu_v2_typed_free", [&] { delete t; });
+}
+
 __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_free(FaberGpuQ4kTensor* t) {
   return guarded("faber_gpu_v2_q4k_free", [&] { delete t; });
 }

@@ -97,3 +97,30 @@ def device_ptr(logical_id: int) -> tuple[int, int]:
     p, n = ctypes.c_void_p(), _lib.U64()
     _lib.call("faber_gpu_v2_buffer_device_ptr", logical_id, ctypes.byref(p), ctypes.byref(n))
     return p.value or 0, n.value
+
+
+class TypedTensor:
+    """A linear of any admitted block type as typed rows (the row GEMV of
+    the decoder's non-Q4_K linears)."""
+
+    def __init__(self, ggml_type: int, host_blocks: np.ndarray, rows: int, cols: int):
+        b = np.ascontiguousarray(host_blocks, dtype=np.uint8)
+        h = ctypes.c_void_p()
+        _lib.call("faber_gpu_v2_typed_upload", ggml_type, b.ctypes.data, b.nbytes, rows, cols,
+                  ctypes.byref(h))
+        self._h = h
+        self.rows, self.cols = rows, cols
+
+    def gemv(self, x_ptr: int, y_ptr: int, stream: int = 0) -> None:
+        _lib.call("faber_gpu_v2_typed_gemv", self._h, x_ptr, y_ptr, stream)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.call("faber_gpu_v2_typed_free", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -125,6 +125,17 @@ FaberRtStatusV1 faber_gpu_v2_dequant_q4k(const uint8_t* blocks, uint64_t n_block
 FaberRtStatusV1 faber_gpu_v2_dequant_blocks(uint32_t ggml_type, const uint8_t* blocks,
                                             uint64_t n_blocks, float* out, int32_t f16_round,
                                             void* stream);
+/* A linear of any admitted block type (Q4_K, Q6_K, Q5_0, Q8_0, F32, F16),
+ * uploaded as typed rows, and y = dense(W, x) through the row GEMV that
+ * serves the decoder's non-Q4_K linears (dense, src/decoder_ops.rs:378-406,
+ * with f16-rounded weights, src/cpu_oracle.rs:356-360). */
+typedef struct FaberGpuTypedTensor FaberGpuTypedTensor;
+FaberRtStatusV1 faber_gpu_v2_typed_upload(uint32_t ggml_type, const uint8_t* host_blocks,
+                                          uint64_t nbytes, uint64_t rows, uint64_t cols,
+                                          FaberGpuTypedTensor** out);
+FaberRtStatusV1 faber_gpu_v2_typed_gemv(const FaberGpuTypedTensor* t, const float* x, float* y,
+                                        void* stream);
+FaberRtStatusV1 faber_gpu_v2_typed_free(FaberGpuTypedTensor* t);
 
 /* f32 -> f16 (round-to-nearest-even) -> f32, element-wise: kv_f16_round
  * (src/cpu_oracle.rs:225-294). */

@@ -243,3 +243,31 @@ def test_dequant_other_block_types_bit_exact(cuda, oracle, gtype):
     dequant.dequant_blocks(gtype, d.data_ptr(), n, out.data_ptr(), f16_round=True)
     torch.cuda.synchronize()
     same_bits(out.cpu().numpy(), oracle.f16_round(ref))
+
+
+TYPED_SHAPES = [(14, 4096, 4096), (14, 64, 11008), (8, 300, 1536), (6, 100, 512), (12, 33, 1024)]
+
+
+@pytest.mark.parametrize("gtype,rows,cols", TYPED_SHAPES)
+def test_typed_row_gemv_matches_oracle(cuda, oracle, gtype, rows, cols):
+    """The row GEMV (Q6_K, Q8_0, Q5_0 and Q4_K rows) against the oracle's
+    dense with f16-rounded weights: within 1e-4 x RMS (f32 sums in another
+    order), including ragged tiles (rows not a multiple of 16)."""
+    from faber_runtime_b200 import dequant, synth
+    be, bb, at = {6: (32, 22, 0), 8: (32, 34, 0), 12: (256, 144, 0), 14: (256, 210, 208)}[gtype]
+    n = rows * cols // be
+    if gtype == 12:
+        blocks = synth.q4k_blocks(31, rows + cols, n)
+    else:
+        rng = np.random.default_rng(rows * 7 + cols)
+        b = rng.integers(0, 256, (n, bb), dtype=np.uint8)
+        b[:, at:at + 2] = rng.uniform(1e-3, 2e-2, n).astype(np.float16).view(np.uint8).reshape(n, 2)
+        blocks = b.reshape(-1)
+    x = synth.normal(31, cols, cols)
+    ref = oracle.dense_q(gtype, blocks, x, cols, rows, f16_round=True)
+    t = dequant.TypedTensor(gtype, blocks, rows, cols)
+    y = torch.full((rows,), float("nan"), dtype=torch.float32, device=cuda)
+    t.gemv(to_dev(x).data_ptr(), y.data_ptr())
+    torch.cuda.synchronize()
+    assert within(y.cpu().numpy(), ref) < 1e-4
+    t.close()
