@@ -1,7 +1,7 @@
 // attention.cuh — split-K GQA decode attention over the f16 KV cache
 // (attention_gqa, src/cpu_oracle.rs:711-792, for one query row).
 //
-// Grid (kv_heads, splits), splits fixed per session (about three CTAs per SM
+// Grid (kv_heads, splits), splits fixed per session (about six CTAs per SM
 // over all kv heads). CTA (kv head kh, split s) covers an equal share of the
 // current context, in groups of 32 positions (8 per warp), for the `ratio`
 // query heads that share kv head kh (h / ratio == kh, the reference's
@@ -33,7 +33,7 @@ constexpr int kAttnRows = 8;                         // rows per warp per group
 constexpr int kAttnGroup = kAttnRows * kAttnWarps;   // 32 positions per CTA group
 constexpr int kAttnMaxRatio = 8;
 constexpr int kAttnMergeBatch = 16;
-constexpr int kAttnCtasPerSm = 3;
+constexpr int kAttnCtasPerSm = 6;  // splits: ~6 per SM over all kv heads (4 resident by registers; finer shares balance the waves)
 
 struct AttnArgs {
   const float* q;          // [H][hd] post-RoPE queries
