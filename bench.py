@@ -21,14 +21,20 @@ e2e        tokens/s through the public API with host buffers: per token
 roofline   the Q4_K dequant-GEMV (the dominant kernel) over this rank's
            7B layer shapes + head, replayed in a CUDA graph over three
            weight copies per shape (411 MB > L2), CUDA events.
+prefill_batch8   eight more 2048-id prompts through the prompt pass, one
+           after another (one GPU; wall clock, tokens/s).
+decode_batch16   sixteen sessions with their own prompts decoding K greedy
+           tokens together through the batched path (one GPU; CUDA events;
+           aggregate tokens/s). --no-batch skips both legs.
 cpu_baseline  the C++ oracle restatement of the reference's CPU path on
            this host's cores: a 2-layer sample of the same model at
            context 2048, extrapolated to 32 layers.
 
 --impl reference times that CPU path as its own line (the reference is
 Rust with no toolchain here; its restatement is the oracle port).
-Multi-GPU (torchrun): tensor parallel over N ranks with NCCL all-reduce
-after the O and down projections; same tokens on every rank.
+Multi-GPU (torchrun): tensor parallel over N ranks, the O and down partial
+sums exchanged over NVLink peer memory inside the GEMVs; same tokens on
+every rank.
 """
 
 from __future__ import annotations
@@ -382,6 +388,8 @@ def run_faber(args):
             "prefill": prefill_line(cfg, PREFILL, prefill_s, ws),
             "greedy_all_finite": bool(finite),
             "clocks": clk.summary()}
+    if ws == 1 and not args.no_batch:
+        line["prefill_batch8"], line["decode_batch16"] = batch_legs(cfg, model, args)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(cfg)
     if rank == 0:
@@ -391,6 +399,42 @@ def run_faber(args):
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+
+
+def batch_legs(cfg, model, args):
+    """Batch-8 prompt pass and batch-16 decode (one GPU): 16 sessions, each
+    with its own 2048-id prompt; the first 8 prompts are timed (sequences
+    after one another through the tensor-core prompt pass), then all 16
+    decode together through the batched path (every weight read once per
+    step for the 16 sequences), CUDA events around the greedy steps."""
+    import torch
+    from faber_runtime_b200 import BatchRun, ForwardRun, synth
+    ctx = PREFILL + args.warmup + args.steps + 8
+    runs = [ForwardRun(model, context_length=ctx) for _ in range(16)]
+    prompts = [synth.tokens(SEED, 100 + i, PREFILL, cfg.vocab) for i in range(16)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for r, p in zip(runs[:8], prompts[:8]):
+        r.push_tokens(p)
+    torch.cuda.synchronize()
+    pf_s = time.perf_counter() - t0
+    for r, p in zip(runs[8:], prompts[8:]):
+        r.push_tokens(p)
+    batch = BatchRun(runs)
+    batch.greedy(args.warmup)
+    torch.cuda.synchronize()
+    _, fin = batch.greedy(args.steps)
+    ms = batch.last_ms()
+    batch.close()
+    for r in runs:
+        r.close()
+    flop = 2.0 * (cfg.linear_bytes() * 256 / 144) * 8 * PREFILL
+    return ({"sequences": 8, "tokens": 8 * PREFILL, "ms": pf_s * 1e3, "tok_s": 8 * PREFILL / pf_s,
+             "linear_tflops_useful": flop / pf_s / 1e12, "path": "tensor-core prompt pass per sequence"},
+            {"sequences": 16, "steps": args.steps, "ms_per_step": ms / args.steps,
+             "tok_s": 16 * args.steps / (ms * 1e-3), "all_finite": bool(fin.all()),
+             "path": "batched tcgen05 Q4_K GEMMs, per-sequence attention",
+             "context": f"{PREFILL} + up to {args.warmup + args.steps}"})
 
 
 def ctypes_uid() -> bytes:
@@ -409,6 +453,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--impl", default="faber", choices=["faber", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch", action="store_true", help="skip the batch-8 prompt and batch-16 decode legs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
