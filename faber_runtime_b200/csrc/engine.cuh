@@ -236,6 +236,30 @@ void launch_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pd
     launch_pdl(attention_decode_kernel<HD, 8>, grid, block, 0, stream, pdl, a);
 }
 
+// Decode attention of a step: grouped heads (ratio 3..8) on the tensor cores,
+// one wave of CTAs (kv heads x sequences x splits, the split count within the
+// session's partial buffer); other ratios on the CUDA-core kernel.
+template <int HD>
+void launch_decode_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pdl) {
+  const int ratio = a.n_heads / a.n_kv_heads;
+  if (ratio < 3 || ratio > 8) {
+    launch_attention<HD>(a, grid, stream, pdl);
+    return;
+  }
+  auto kern = attention_tc_kernel<HD>;
+  static thread_local std::map<int, bool> attr_done;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gqa_smem_bytes<HD>()));
+    attr_done[dev] = true;
+  }
+  const int kv = (int)(grid.x * grid.z);
+  const int want = std::max(1, kGqaCtasPerSm * device_info().sms / kv);
+  const dim3 g(grid.x, std::min((int)grid.y, want), grid.z);
+  launch_pdl(kern, g, dim3(128), gqa_smem_bytes<HD>(), stream, pdl, a);
+}
+
 // ---------------------------------------------------------------------------
 // Model construction
 // ---------------------------------------------------------------------------
@@ -768,9 +792,9 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       a.scale = 1.0f / sqrtf((float)hd);
       const dim3 grid(M.Hkvl, S.max_splits);
       if (hd == 128)
-        launch_attention<128>(a, grid, S.stream, pdl);
+        launch_decode_attention<128>(a, grid, S.stream, pdl);
       else
-        launch_attention<64>(a, grid, S.stream, pdl);
+        launch_decode_attention<64>(a, grid, S.stream, pdl);
       if (tr) FABER_CUDA(cudaMemcpyAsync(tr + 4 * S.tr_w, S.ctx.p, nq * 4, cudaMemcpyDeviceToDevice, S.stream));
     }
     // O projection (+ residual)
@@ -1439,9 +1463,9 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.slot_counter_stride = M.Hkvl;
       const dim3 grid(M.Hkvl, Bt.splits, n);
       if (hd == 128)
-        launch_attention<128>(a, grid, Bt.stream, false);
+        launch_decode_attention<128>(a, grid, Bt.stream, false);
       else
-        launch_attention<64>(a, grid, Bt.stream, false);
+        launch_decode_attention<64>(a, grid, Bt.stream, false);
     }
     prefill_split_kernel<false><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.ctx.as<float>(), nq, nullptr, 0.0f,
                                                                     xs, xscale);

@@ -30,6 +30,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "ops.cuh"
@@ -843,7 +844,7 @@ __global__ void __launch_bounds__(kFaThreads) prefill_flash_kernel(const float* 
         mma16816(o_acc[2 * dp + 1], pl, b[2], b[3]);
       }
     }
-    __syncthreads();  // the next iteration's load overwrites this stage
+    __syncthreads();  // the next iteration's load (or the merge rows) overwrites this stage
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -857,6 +858,290 @@ __global__ void __launch_bounds__(kFaThreads) prefill_flash_kernel(const float* 
     if (t0 < n) *reinterpret_cast<float2*>(out0 + 8 * i) = make_float2(o_acc[i][0] * inv0, o_acc[i][1] * inv0);
     if (t0 + 8 < n) *reinterpret_cast<float2*>(out1 + 8 * i) = make_float2(o_acc[i][2] * inv1, o_acc[i][3] * inv1);
   }
+}
+
+
+// ---- grouped-query decode attention on the tensor cores ---------------------
+//
+// attention_gqa (src/cpu_oracle.rs:711-792) for one query row per sequence
+// when several query heads share a kv head (ratio 3..8): the ratio's query
+// heads form the 16-row M tile of m16n8k16 MMAs (rows past the ratio are
+// zero), the cached keys the N dimension, so each K/V byte feeds every head
+// of the group at once. CTA = (kv head, split, sequence), 4 warps; the
+// split's keys go in tiles of 64, double-buffered by cp.async into
+// XOR-swizzled shared memory, and each warp takes 16 keys of a tile:
+//   * S = Q K^T with Q split exactly into hi/lo f16 (a power-of-two scale per
+//     head), K f16 from the cache; score = (q . k) * scale;
+//   * an online softmax per head row (running max and sum), P split into
+//     hi/lo f16 for O += P V;
+//   * the 4 warps' states combine in shared memory into the split's
+//     (max, sum, context) partial, the same format and the same last-CTA
+//     merge in split order as attention_decode_kernel.
+constexpr int kGqaKeys = 64;
+
+constexpr int kGqaCtasPerSm = 3;
+
+// Q hi/lo rows, then two stages of K and V; after the key loop the stages
+// hold the per-warp context rows (ratio <= 8) and (max, sum) pairs.
+template <int HD>
+__host__ __device__ constexpr int gqa_smem_bytes() {
+  static_assert(4 * 8 * HD * 4 + 4 * 8 * 2 * 4 <= 2 * 2 * kGqaKeys * HD * 2, "merge rows fit the stages");
+  return 2 * 16 * HD * 2 + 2 * 2 * kGqaKeys * HD * 2;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128, kGqaCtasPerSm) attention_tc_kernel(const AttnArgs a0) {
+  const AttnArgs a = slot_args(a0);
+  constexpr int CH = HD / 8;
+  extern __shared__ __align__(128) unsigned char gq_smem[];
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(gq_smem);
+  const uint32_t qh_base = sbase, ql_base = sbase + 16 * HD * 2;
+  const uint32_t kv_base = sbase + 2 * 16 * HD * 2;
+  float* red = reinterpret_cast<float*>(gq_smem + 2 * 16 * HD * 2);  // aliases the K/V stages
+  float* wst = red + 4 * 8 * HD;
+  __shared__ int qshift[16];
+  __shared__ int is_last;
+
+  const int kh = blockIdx.x, split = blockIdx.y;
+  const int ratio = a.n_heads / a.n_kv_heads;  // 3..8
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();  // the step's own K/V row and q come from the preceding kernel
+  pdl_launch_dependents();
+  const int cur = a.st->cur_pos, n_kv = cur + 1;
+  const int n_tiles = (n_kv + kGqaKeys - 1) / kGqaKeys;
+  const int per = (n_tiles + gridDim.y - 1) / gridDim.y;
+  const int active = (n_tiles + per - 1) / per;
+  const int t0 = split * per, t1 = min(n_tiles, t0 + per);
+  if (t0 >= t1) return;
+  const size_t kvs = (size_t)a.n_kv_heads * HD;
+  const __half* kh_k = a.k + (size_t)kh * HD;
+  const __half* kh_v = a.v + (size_t)kh * HD;
+
+  auto load_tile = [&](int t, int stage) {
+    const uint32_t kdst = kv_base + (uint32_t)(2 * stage) * (kGqaKeys * HD * 2);
+    const uint32_t vdst = kdst + kGqaKeys * HD * 2;
+#pragma unroll
+    for (int i = 0; i < kGqaKeys * CH / 128; ++i) {
+      const int c = tid + i * 128;
+      const int row = c / CH, ch = c % CH;
+      const int key = t * kGqaKeys + row;
+      const bool valid = key < n_kv;
+      const size_t off = (size_t)(valid ? key : 0) * kvs + (size_t)ch * 8;
+      cp_async16(kdst + fa_off<HD>(row, ch), kh_k + off, valid);
+      cp_async16(vdst + fa_off<HD>(row, ch), kh_v + off, valid);
+    }
+    cp_async_commit();
+  };
+  load_tile(t0, 0);
+
+  // Q rows: head kh * ratio + r for r < ratio, zero past it; per-row
+  // power-of-two scale and exact hi/lo split (4 rows per warp)
+  {
+    constexpr int PL = HD / 32;
+    for (int rr = 0; rr < 4; ++rr) {
+      const int r = warp * 4 + rr;
+      float v[PL];
+#pragma unroll
+      for (int i = 0; i < PL; ++i) v[i] = 0.0f;
+      if (r < ratio) {  // only this kv head's query rows are read
+        const float* src = a.q + (size_t)(kh * ratio + r) * HD + lane * PL;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) v[i] = src[i];
+      }
+      float mx = 0.0f;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) mx = fmaxf(mx, fabsf(v[i]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const int sh = split_shift(mx);
+      const float in_s = ldexpf(1.0f, -sh);
+      if (lane == 0) qshift[r] = sh;
+      uint32_t hb[PL / 2], lb[PL / 2];
+#pragma unroll
+      for (int i = 0; i < PL / 2; ++i) split2(v[2 * i] * in_s, v[2 * i + 1] * in_s, hb[i], lb[i]);
+      const uint32_t o = fa_off<HD>(r, (lane * PL) / 8) + (uint32_t)((lane * PL) % 8) * 2;
+      if constexpr (PL == 4) {
+        asm volatile("st.shared.v2.b32 [%0], {%1,%2};\n" ::"r"(qh_base + o), "r"(hb[0]), "r"(hb[1]));
+        asm volatile("st.shared.v2.b32 [%0], {%1,%2};\n" ::"r"(ql_base + o), "r"(lb[0]), "r"(lb[1]));
+      } else {
+        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(qh_base + o), "r"(hb[0]));
+        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(ql_base + o), "r"(lb[0]));
+      }
+    }
+  }
+  __syncthreads();
+  const float f0 = ldexpf(a.scale, qshift[lane >> 2]), f1 = ldexpf(a.scale, qshift[(lane >> 2) + 8]);
+  float o_acc[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  const int mi = lane >> 3, r8 = lane & 7;
+
+  for (int t = t0; t < t1; ++t) {
+    const int stage = (t - t0) & 1;
+    if (t + 1 < t1) {
+      load_tile(t + 1, stage ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t kbase = kv_base + (uint32_t)(2 * stage) * (kGqaKeys * HD * 2);
+    const uint32_t vbase = kbase + kGqaKeys * HD * 2;
+    // S = Q K^T over this warp's 16 keys: 2 tiles of 16 heads x 8 keys
+    float sacc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      uint32_t ah[4], al[4], b[4];
+      const uint32_t qo = fa_off<HD>((mi & 1) * 8 + r8, 2 * kk + (mi >> 1));
+      ldsm_x4(qh_base + qo, ah);
+      ldsm_x4(ql_base + qo, al);
+      ldsm_x4(kbase + fa_off<HD>(warp * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
+      mma16816(sacc[0], ah, b[0], b[1]);
+      mma16816(sacc[1], ah, b[2], b[3]);
+      mma16816(sacc[0], al, b[0], b[1]);
+      mma16816(sacc[1], al, b[2], b[3]);
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = t * kGqaKeys + warp * 16 + nt * 8 + 2 * (lane & 3) + e;
+        const float x0 = key < n_kv ? sacc[nt][e] * f0 : -INFINITY;
+        const float x1 = key < n_kv ? sacc[nt][2 + e] * f1 : -INFINITY;
+        sacc[nt][e] = x0;
+        sacc[nt][2 + e] = x1;
+        mx0 = fmaxf(mx0, x0);
+        mx1 = fmaxf(mx1, x1);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float base0 = mn0 == -INFINITY ? 0.0f : mn0, base1 = mn1 == -INFINITY ? 0.0f : mn1;
+    const float c0 = expf(m0 - base0), c1 = expf(m1 - base1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sacc[nt][e] = expf(sacc[nt][e] - base0);
+        sacc[nt][2 + e] = expf(sacc[nt][2 + e] - base1);
+        ps0 += sacc[nt][e];
+        ps1 += sacc[nt][2 + e];
+      }
+    }
+    l0 = fmaf(l0, c0, ps0);
+    l1 = fmaf(l1, c1, ps1);
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) {
+      o_acc[i][0] *= c0;
+      o_acc[i][1] *= c0;
+      o_acc[i][2] *= c1;
+      o_acc[i][3] *= c1;
+    }
+    // O += P V over the warp's 16 keys (one k-step)
+    uint32_t ph[4], pl[4];
+    split2(sacc[0][0], sacc[0][1], ph[0], pl[0]);
+    split2(sacc[0][2], sacc[0][3], ph[1], pl[1]);
+    split2(sacc[1][0], sacc[1][1], ph[2], pl[2]);
+    split2(sacc[1][2], sacc[1][3], ph[3], pl[3]);
+#pragma unroll
+    for (int dp = 0; dp < HD / 16; ++dp) {
+      uint32_t b[4];
+      ldsm_x4_t(vbase + fa_off<HD>(warp * 16 + (mi & 1) * 8 + r8, 2 * dp + (mi >> 1)), b);
+      mma16816(o_acc[2 * dp], ph, b[0], b[1]);
+      mma16816(o_acc[2 * dp + 1], ph, b[2], b[3]);
+      mma16816(o_acc[2 * dp], pl, b[0], b[1]);
+      mma16816(o_acc[2 * dp + 1], pl, b[2], b[3]);
+    }
+    __syncthreads();  // the next iteration's load (or the merge rows) overwrites this stage
+  }
+  // this warp's state for head rows r < ratio (rows lane/4; rows + 8 are padding)
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  const int r = lane >> 2;
+  if (r < ratio) {
+    if ((lane & 3) == 0) {
+      wst[(warp * 8 + r) * 2] = m0;
+      wst[(warp * 8 + r) * 2 + 1] = l0;
+    }
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) {
+      red[(warp * 8 + r) * HD + 8 * i + 2 * (lane & 3)] = o_acc[i][0];
+      red[(warp * 8 + r) * HD + 8 * i + 2 * (lane & 3) + 1] = o_acc[i][1];
+    }
+  }
+  __syncthreads();
+  const int stride = HD + 2;
+  for (int idx = tid; idx < ratio * HD; idx += 128) {
+    const int rr = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wst[(w * 8 + rr) * 2]);
+    float L = 0.0f, sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = wst[(w * 8 + rr) * 2];
+      const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+      L = fmaf(wst[(w * 8 + rr) * 2 + 1], f, L);
+      sum = fmaf(red[(w * 8 + rr) * HD + d], f, sum);
+    }
+    float* pp = a.part + ((size_t)(kh * ratio + rr) * a.max_splits + split) * stride;
+    pp[2 + d] = sum;
+    if (d == 0) {
+      pp[0] = M;
+      pp[1] = L;
+    }
+  }
+  // the last CTA of this kv head merges all splits in split order
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int ticket = atomicAdd(&a.counters[kh], 1);
+    is_last = (ticket == active - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int idx = tid; idx < ratio * HD; idx += 128) {
+    const int rr = idx / HD, d = idx % HD;
+    const float* base = a.part + (size_t)(kh * ratio + rr) * a.max_splits * stride;
+    float M = -INFINITY, L = 0.0f, acc_d = 0.0f;
+    for (int s0 = 0; s0 < active; s0 += kAttnMergeBatch) {
+      float ms[kAttnMergeBatch], ls[kAttnMergeBatch], vs[kAttnMergeBatch];
+#pragma unroll
+      for (int u = 0; u < kAttnMergeBatch; ++u) {
+        const bool ok = s0 + u < active;
+        const float* pq = base + (size_t)(s0 + u) * stride;
+        ms[u] = ok ? __ldcg(pq) : -INFINITY;
+        ls[u] = ok ? __ldcg(pq + 1) : 0.0f;
+        vs[u] = ok ? __ldcg(pq + 2 + d) : 0.0f;
+      }
+      float mb = M;
+#pragma unroll
+      for (int u = 0; u < kAttnMergeBatch; ++u) mb = fmaxf(mb, ms[u]);
+      const float c = expf(M - mb);
+      L *= c;
+      acc_d *= c;
+#pragma unroll
+      for (int u = 0; u < kAttnMergeBatch; ++u) {
+        const float f = expf(ms[u] - mb);
+        L = fmaf(ls[u], f, L);
+        acc_d = fmaf(vs[u], f, acc_d);
+      }
+      M = mb;
+    }
+    a.ctx[(size_t)(kh * ratio + rr) * HD + d] = acc_d / L;
+  }
+  if (tid == 0) a.counters[kh] = 0;
 }
 
 }  // namespace faber
