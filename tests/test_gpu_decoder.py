@@ -227,6 +227,30 @@ def test_prompt_pass_matches_oracle(cuda, which, n_prompt):
     assert fin and toks.tolist() == ref_tokens.tolist()
 
 
+def test_reset_session_reruns_prompt_pass_identically(cuda):
+    """A session reset and the same prompt pushed again through the prompt
+    pass gives bit-identical
+    logits and tokens: the pass reuses the session's scratch, and every
+    reduction (split-K GEMMs, attention splits) runs in a fixed order."""
+    from faber_runtime_b200 import ForwardRun, ModelConfig, synth
+    cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=4, head_dim=64,
+                      ffn=2816, vocab=4096, tied_head=False, rope_theta=500000.0, name="reset-gqa")
+    _, dm, _ = build_pair(cfg, 17, norms="random")
+    prompt = synth.tokens(17, 4, 300, cfg.vocab)
+    run = ForwardRun(dm, context_length=320)
+    run.push_tokens(prompt)
+    first = run.position_logits().copy()
+    toks1, fin1 = run.greedy(4)
+    run.reset()
+    assert len(run) == 0
+    run.push_tokens(prompt)
+    assert np.array_equal(run.position_logits(), first)
+    toks2, fin2 = run.greedy(4)
+    assert fin1 and fin2 and toks1.tolist() == toks2.tolist()
+    run.close()
+    dm.close()
+
+
 def test_fail_closed_and_commit_contract(tiny):
     from faber_runtime_b200 import FaberError, ForwardRun, OracleError
     _, dm, _ = tiny
