@@ -14,9 +14,10 @@ LIB_PATH = Path(__file__).resolve().parent / "libfaber_gpu.so"
 
 OK, INVALID_ARGUMENT, IO_ERROR, PANIC, UNSUPPORTED, FALLIBLE = 0, 1, 2, 3, 4, 5
 TIMEOUT, DEVICE_LOSS, CANCELLED, ALLOCATION, CUDA_ERROR, KERNEL_ERROR = 16, 17, 18, 19, 20, 21
+BUDGET_EXCEEDED = 22
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARGUMENT", 2: "IO_ERROR", 3: "PANIC", 4: "UNSUPPORTED",
                 5: "FALLIBLE", 16: "TIMEOUT", 17: "DEVICE_LOSS", 18: "CANCELLED",
-                19: "ALLOCATION", 20: "CUDA_ERROR", 21: "KERNEL_ERROR"}
+                19: "ALLOCATION", 20: "CUDA_ERROR", 21: "KERNEL_ERROR", 22: "BUDGET_EXCEEDED"}
 
 GGML_F32, GGML_Q5_0, GGML_Q8_0, GGML_Q4_K, GGML_Q6_K = 0, 6, 8, 12, 14
 
@@ -40,6 +41,13 @@ class KvLayoutC(ctypes.Structure):
                 ("layer_count", ctypes.c_uint32), ("kv_head_count", ctypes.c_uint32),
                 ("head_dim", ctypes.c_uint32), ("dtype", ctypes.c_uint32),
                 ("reserve_bytes", ctypes.c_uint64)]
+
+
+class PartitionLedgerC(ctypes.Structure):
+    _fields_ = [("weight_bytes", ctypes.c_uint64), ("kv_cache_bytes", ctypes.c_uint64),
+                ("activation_scratch_bytes", ctypes.c_uint64), ("module_storage_bytes", ctypes.c_uint64),
+                ("allocator_overhead_bytes", ctypes.c_uint64), ("transfer_staging_bytes", ctypes.c_uint64),
+                ("concurrent_state_bytes", ctypes.c_uint64)]
 
 
 class FaberError(RuntimeError):
@@ -78,6 +86,11 @@ SIGNATURES = {
     "faber_gpu_v2_q4k_repack_hash": (Status, [P, ctypes.POINTER(U64)]),
     "faber_gpu_v2_kv_layout_bytes": (Status, [ctypes.POINTER(KvLayoutC), ctypes.POINTER(U64),
                                               ctypes.POINTER(U64)]),
+    "faber_gpu_v2_partition_admit": (Status, [ctypes.POINTER(PartitionLedgerC), U64, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_partition_usage": (Status, [I32, ctypes.POINTER(PartitionLedgerC)]),
+    "faber_gpu_v2_partition_set_limit": (Status, [I32, U64]),
+    "faber_gpu_v2_partition_plan": (Status, [ctypes.POINTER(ModelConfigC), U32, U32, I32,
+                                             ctypes.POINTER(PartitionLedgerC)]),
     "faber_gpu_v2_model_create": (Status, [ctypes.POINTER(ModelConfigC), PP]),
     "faber_gpu_v2_model_set_tensor": (Status, [P, ctypes.c_char_p, U32, P, U64, U64, U64]),
     "faber_gpu_v2_tp_shard": (Status, [ctypes.POINTER(ModelConfigC), ctypes.c_char_p, P]),

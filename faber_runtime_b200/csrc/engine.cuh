@@ -313,6 +313,55 @@ inline TpPlan tp_plan(const FaberModelConfigV1& c) {
   return P;
 }
 
+// Device buffer sizes of one session (session_open's allocations), from the
+// rank's local dimensions. Host-only: the session and the partition plan use
+// the same formulas.
+struct SessionSizes {
+  int max_splits = 0;
+  uint64_t cache = 0;          // each of K and V: [L][ctx][Hkvl*hd] f16
+  uint64_t rope = 0;           // [ctx][hd/2] (cos, sin)
+  uint64_t vec_d = 0;          // each of h, h2, opart, dpart: [d] f32
+  uint64_t vec_q = 0;          // each of q, ctx: [Hl*hd] f32
+  uint64_t hh = 0;             // [Fl] f32
+  uint64_t logits = 0;         // [Vl] f32
+  uint64_t logits_full = 0;    // [V] f32 under tensor parallelism
+  uint64_t attn_part = 0;      // [Hl][splits][hd+2] f32
+  uint64_t attn_counters = 0;  // [Hkvl] i32
+  uint64_t state = 0, gen = 0, prompt = 0;
+  uint64_t tp_buf = 0;         // exchange partials and barrier words
+};
+
+inline SessionSizes session_sizes(const FaberModelConfigV1& c, int Hl, int Hkvl, int Fl, int Vl,
+                                  int max_ctx, int sms) {
+  SessionSizes z;
+  const uint64_t hd = c.head_dim, d = c.d_model, ctx = (uint64_t)max_ctx, tp = c.tp_size;
+  z.max_splits = attention_splits(sms, Hkvl, max_ctx);
+  z.cache = (uint64_t)c.n_layers * ctx * ((uint64_t)Hkvl * hd) * 2;
+  z.rope = ctx * (hd / 2) * sizeof(float2);
+  z.vec_d = d * 4;
+  z.vec_q = (uint64_t)Hl * hd * 4;
+  z.hh = (uint64_t)Fl * 4;
+  z.logits = (uint64_t)Vl * 4;
+  z.logits_full = tp > 1 ? (uint64_t)c.vocab * 4 : 0;
+  z.attn_part = (uint64_t)Hl * (uint64_t)z.max_splits * (hd + 2) * 4;
+  z.attn_counters = (uint64_t)Hkvl * 4;
+  z.state = sizeof(StepState);
+  z.gen = ctx * 8 + 8;
+  z.prompt = ctx * 8;
+  z.tp_buf = tp > 1 ? 2 * tp * d * sizeof(unsigned long long) + 256 : 0;
+  return z;
+}
+
+// Prompt-pass scratch of a session for chunks of up to cap tokens.
+struct PrefillSizes {
+  uint64_t h, xs, scale, q, ctx, act;
+};
+
+inline PrefillSizes prefill_sizes(uint64_t d, uint64_t nq, uint64_t F, uint64_t cap) {
+  const uint64_t kmax = std::max(d, std::max(nq, F));
+  return {cap * d * 4, 2 * cap * kmax * 2, cap * 4, cap * nq * 4, cap * nq * 4, cap * F * 4};
+}
+
 // Full shape of a named tensor and this rank's block [r0, r0+nr) x [c0, c0+nc).
 struct ShardRange {
   uint64_t rows = 0, cols = 0, r0 = 0, nr = 0, c0 = 0, nc = 0;
@@ -494,9 +543,9 @@ inline void rows_from(DeviceRows& D, int rows, int cols, PartOf part_of) {
     const uint64_t rb = (uint64_t)cols / be * bb;
     std::memcpy(bytes.data() + off[j], pr.first->bytes.data() + pr.second * rb, rb);
   }
-  upload(D.bytes, bytes.data(), bytes.size());
-  upload(D.row_off, off.data(), off.size() * 8);
-  upload(D.row_type, type.data(), type.size() * 4);
+  upload(D.bytes, bytes.data(), bytes.size(), kLedgerWeights);
+  upload(D.row_off, off.data(), off.size() * 8, kLedgerWeights);
+  upload(D.row_type, type.data(), type.size() * 4, kLedgerWeights);
   D.n_tiles = n_tiles;
   D.rows = rows;
   D.cols = cols;
@@ -572,7 +621,7 @@ inline void model_finalize(ModelState& M) {
       std::vector<float> w(d);
       std::memcpy(w.data(), S[(size_t)k].bytes.data(), d * 4);
       for (auto& v : w) v = host_f16_round(v);
-      upload(k == LS_ATTN_NORM ? L.attn_norm : L.ffn_norm, w.data(), d * 4);
+      upload(k == LS_ATTN_NORM ? L.attn_norm : L.ffn_norm, w.data(), d * 4, kLedgerWeights);
     }
     bytes += L.qkv.w.n + L.o.w.n + L.gateup.w.n + L.down.w.n + 2 * d * 4;
     bytes += L.qkv_r.bytes.n + L.o_r.bytes.n + L.gateup_r.bytes.n + L.down_r.bytes.n;
@@ -586,11 +635,11 @@ inline void model_finalize(ModelState& M) {
     const uint64_t n = (uint64_t)c.vocab * d;
     std::vector<uint16_t> h(n);
     for (uint64_t i = 0; i < n; ++i) h[i] = host_f32_to_f16(e[i]);
-    upload(M.embd_f16, h.data(), n * 2);
+    upload(M.embd_f16, h.data(), n * 2, kLedgerWeights);
     bytes += n * 2;
     std::vector<uint8_t>().swap(M.st_embd.bytes);
   }
-  upload(M.out_norm, M.st_out_norm.bytes.data(), d * 4);  // not rounded (src/cpu_oracle.rs:434)
+  upload(M.out_norm, M.st_out_norm.bytes.data(), d * 4, kLedgerWeights);  // not rounded (src/cpu_oracle.rs:434)
   if (!c.tied_head && M.st_output.type != FABER_GGML_Q4_K) {
     rows_from(M.head_r, (int)M.st_output.rows, (int)d, [&](int j) {
       return std::pair<const HostTensor*, uint64_t>(&M.st_output, (uint64_t)j);
@@ -617,13 +666,14 @@ inline void model_finalize(ModelState& M) {
 // every rank's zeroing before any peer can store into its buffer.
 inline void open_tp_exchange(SessionState& S) {
   ModelState& M = S.m->s;
-  const size_t tp = (size_t)M.tp, d = M.cfg.d_model;
+  const size_t tp = (size_t)M.tp;
   // partials, then the grid-barrier words of the consuming kernels
-  S.tp_buf.alloc(2 * tp * d * sizeof(unsigned long long) + 256);
+  S.tp_buf.alloc(session_sizes(M.cfg, M.Hl, M.Hkvl, M.Fl, M.Vl, S.max_ctx, device_info().sms).tp_buf,
+                kLedgerStaging);
   FABER_CUDA(cudaMemset(S.tp_buf.p, 0, S.tp_buf.n));  // epoch 0 never matches
   cudaIpcMemHandle_t mine;
   FABER_CUDA(cudaIpcGetMemHandle(&mine, S.tp_buf.p));
-  DevBuf hb(sizeof(cudaIpcMemHandle_t) * tp);
+  DevBuf hb(sizeof(cudaIpcMemHandle_t) * tp, kLedgerStaging);
   unsigned char* slot = hb.as<unsigned char>() + sizeof(mine) * (size_t)M.rank;
   FABER_CUDA(cudaMemcpy(slot, &mine, sizeof(mine), cudaMemcpyHostToDevice));
   FABER_NCCL(ncclAllGather(slot, hb.p, sizeof(mine), ncclUint8, M.comm, S.stream));
@@ -682,14 +732,13 @@ inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV
   S.device = M.device;
   FABER_CUDA(cudaSetDevice(M.device));
   S.max_ctx = (int)kv.context_length;
-  S.max_splits = attention_splits(device_info().sms, M.Hkvl, S.max_ctx);
-  const uint64_t hd = c.head_dim, d = c.d_model;
-  const uint64_t kvs = (uint64_t)M.Hkvl * hd;
-  const uint64_t cache = (uint64_t)c.n_layers * S.max_ctx * kvs * 2;
-  S.kcache.alloc(cache);
-  S.vcache.alloc(cache);
-  FABER_CUDA(cudaMemset(S.kcache.p, 0, cache));
-  FABER_CUDA(cudaMemset(S.vcache.p, 0, cache));
+  const SessionSizes Z = session_sizes(c, M.Hl, M.Hkvl, M.Fl, M.Vl, S.max_ctx, device_info().sms);
+  S.max_splits = Z.max_splits;
+  const uint64_t hd = c.head_dim;
+  S.kcache.alloc(Z.cache, kLedgerKv);
+  S.vcache.alloc(Z.cache, kLedgerKv);
+  FABER_CUDA(cudaMemset(S.kcache.p, 0, Z.cache));
+  FABER_CUDA(cudaMemset(S.vcache.p, 0, Z.cache));
   // RoPE table on the host with the same libm calls as rope_norm
   // (src/decoder_ops.rs:178-186): theta = pos * base^(-(2k)/dim).
   {
@@ -699,27 +748,27 @@ inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV
         const float theta = (float)p * powf(c.rope_theta, -(2.0f * (float)k) / (float)hd);
         t[(size_t)p * (hd / 2) + k] = make_float2(cosf(theta), sinf(theta));
       }
-    upload(S.rope, t.data(), t.size() * sizeof(float2));
+    FABER_ARG(t.size() * sizeof(float2) == Z.rope, "RoPE table size");
+    upload(S.rope, t.data(), Z.rope, kLedgerConcurrent);
   }
-  const uint64_t qn = (uint64_t)M.Hl * hd;
-  S.h.alloc(d * 4);
-  S.h2.alloc(d * 4);
-  S.opart.alloc(d * 4);
-  S.dpart.alloc(d * 4);
-  S.q.alloc(qn * 4);
-  S.ctx.alloc(qn * 4);
-  S.hh.alloc((uint64_t)M.Fl * 4);
-  S.logits.alloc((uint64_t)M.Vl * 4);
-  if (M.tp > 1) S.logits_full.alloc((uint64_t)c.vocab * 4);
-  S.attn_part.alloc((uint64_t)M.Hl * S.max_splits * (hd + 2) * 4);
-  S.attn_counters.alloc((uint64_t)M.Hkvl * 4);
+  S.h.alloc(Z.vec_d);
+  S.h2.alloc(Z.vec_d);
+  S.opart.alloc(Z.vec_d);
+  S.dpart.alloc(Z.vec_d);
+  S.q.alloc(Z.vec_q);
+  S.ctx.alloc(Z.vec_q);
+  S.hh.alloc(Z.hh);
+  S.logits.alloc(Z.logits);
+  if (M.tp > 1) S.logits_full.alloc(Z.logits_full);
+  S.attn_part.alloc(Z.attn_part);
+  S.attn_counters.alloc(Z.attn_counters);
   FABER_CUDA(cudaMemset(S.attn_counters.p, 0, S.attn_counters.n));
-  S.state.alloc(sizeof(StepState));
+  S.state.alloc(Z.state, kLedgerConcurrent);
   StepState st = {};
   st.finite = 1;
   FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
-  S.gen.alloc((uint64_t)S.max_ctx * 8 + 8);
-  S.prompt.alloc((uint64_t)S.max_ctx * 8);
+  S.gen.alloc(Z.gen, kLedgerConcurrent);
+  S.prompt.alloc(Z.prompt, kLedgerConcurrent);
   FABER_CUDA(cudaStreamCreateWithFlags(&S.stream, cudaStreamNonBlocking));
   FABER_CUDA(cudaEventCreate(&S.ev0));
   FABER_CUDA(cudaEventCreate(&S.ev1));
@@ -1053,14 +1102,13 @@ inline void ensure_prefill_scratch(SessionState& S, int cap) {
   if (S.pf_cap >= cap) return;
   ModelState& M = S.m->s;
   const FaberModelConfigV1& c = M.cfg;
-  const size_t d = c.d_model, nq = (size_t)M.Hl * c.head_dim, F = M.Fl;
-  const size_t kmax = std::max(d, std::max(nq, F));
-  S.pf_h.alloc((size_t)cap * d * 4);
-  S.pf_xs.alloc((size_t)2 * cap * kmax * 2);
-  S.pf_scale.alloc((size_t)cap * 4);
-  S.pf_q.alloc((size_t)cap * nq * 4);
-  S.pf_ctx.alloc((size_t)cap * nq * 4);
-  S.pf_act.alloc((size_t)cap * F * 4);
+  const PrefillSizes z = prefill_sizes(c.d_model, (uint64_t)M.Hl * c.head_dim, (uint64_t)M.Fl, (uint64_t)cap);
+  S.pf_h.alloc(z.h);
+  S.pf_xs.alloc(z.xs);
+  S.pf_scale.alloc(z.scale);
+  S.pf_q.alloc(z.q);
+  S.pf_ctx.alloc(z.ctx);
+  S.pf_act.alloc(z.act);
   S.pf_cap = cap;
 }
 
@@ -1349,7 +1397,7 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
       refs[(size_t)l * n + i] = SlotRef{st_ptr(S), S.kcache.as<__half>() + l * layer_cache,
                                         S.vcache.as<__half>() + l * layer_cache};
     }
-  Bt.slots.alloc(refs.size() * sizeof(SlotRef));
+  Bt.slots.alloc(refs.size() * sizeof(SlotRef), kLedgerConcurrent);
   FABER_CUDA(cudaMemcpy(Bt.slots.p, refs.data(), Bt.slots.n, cudaMemcpyHostToDevice));
   const size_t kmax = std::max((size_t)d, std::max((size_t)nq, (size_t)M.Fl));
   Bt.h.alloc((size_t)n * d * 4);
@@ -1367,7 +1415,7 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   Bt.attn_counters.alloc((size_t)n * M.Hkvl * 4);
   FABER_CUDA(cudaMemset(Bt.attn_counters.p, 0, Bt.attn_counters.n));
   Bt.gen_cap = Bt.max_ctx;
-  Bt.gen.alloc((size_t)n * Bt.gen_cap * 8);
+  Bt.gen.alloc((size_t)n * Bt.gen_cap * 8, kLedgerConcurrent);
   size_t part = 0, tiles = 0;
   auto need = [&](const DeviceTiled& W) {
     const size_t m_tiles = (W.rows + kPgBM - 1) / kPgBM;
@@ -1606,6 +1654,95 @@ inline void set_prefix(SessionState& S, uint32_t layer, const float* k, const fl
   FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
 }
 
+// The device buffers of a tiled Q4_K linear whose row j starts at element
+// start(j) of its source: repack_q4k groups rows by their offset inside a
+// super-block, 16 rows per tile, and keeps a tile offset and row map unless
+// every row starts on a block boundary.
+inline void plan_tiled(std::vector<std::pair<uint64_t, int>>& bufs, uint64_t rows, uint64_t cols,
+                       const std::function<uint64_t(uint64_t)>& start) {
+  std::map<uint64_t, uint64_t> per_offset;
+  uint64_t max_o = 0;
+  for (uint64_t j = 0; j < rows; ++j) {
+    const uint64_t o = start(j) % kQ4kBlockElems;
+    ++per_offset[o];
+    max_o = std::max(max_o, o);
+  }
+  uint64_t tiles = 0;
+  for (const auto& kv : per_offset) tiles += (kv.second + kTileRows - 1) / kTileRows;
+  const uint64_t nb = (cols + max_o + kQ4kBlockElems - 1) / kQ4kBlockElems;
+  bufs.push_back({tiles * nb * kTileItemBytes, kLedgerWeights});
+  if (!(per_offset.size() == 1 && per_offset.begin()->first == 0)) {
+    bufs.push_back({tiles * 4, kLedgerWeights});
+    bufs.push_back({tiles * kTileRows * 4, kLedgerWeights});
+  }
+}
+
+// The ledger one rank's model and `sessions` sessions of context_length
+// positions draw on a device with `sms` SMs, before anything is allocated:
+// every buffer the model upload, session_open and (where the prompt pass
+// runs) its scratch allocate, each charged by the allocator policy. Assumes
+// Q4_K linears (the tiled GEMV layout); other block types are charged as
+// they upload.
+inline FaberPartitionLedgerV1 partition_plan(const FaberModelConfigV1& c, uint32_t context_length,
+                                             uint32_t sessions, int sms) {
+  validate_config(c);
+  FABER_ARG(context_length > 0 && sms > 0, "zero context length or SM count");
+  const TpPlan P = tp_plan(c);
+  const uint64_t d = c.d_model, hd = c.head_dim, nq = (uint64_t)P.Hl * hd, nk = (uint64_t)P.Hkvl * hd;
+  const uint64_t fl = (uint64_t)P.Fl;
+  std::vector<std::pair<uint64_t, int>> bufs;
+  // row starts as model_finalize builds them (shards are compact copies)
+  const uint64_t o_cols = c.tp_size == 1 ? (uint64_t)c.n_heads * hd : nq;
+  const uint64_t down_cols = c.tp_size == 1 ? (uint64_t)c.ffn : fl;
+  for (uint32_t l = 0; l < c.n_layers; ++l) {
+    plan_tiled(bufs, nq + 2 * nk, d, [&](uint64_t j) {
+      return (j < nq ? j : (j < nq + nk ? j - nq : j - nq - nk)) * d;
+    });
+    plan_tiled(bufs, d, o_cols, [&](uint64_t j) { return j * o_cols; });
+    plan_tiled(bufs, 2 * fl, d, [&](uint64_t j) { return (j >> 1) * d; });
+    plan_tiled(bufs, d, down_cols, [&](uint64_t j) { return j * down_cols; });
+    bufs.push_back({d * 4, kLedgerWeights});  // attn_norm
+    bufs.push_back({d * 4, kLedgerWeights});  // ffn_norm
+  }
+  bufs.push_back({(uint64_t)c.vocab * d * 2, kLedgerWeights});  // token_embd as f16
+  bufs.push_back({d * 4, kLedgerWeights});                      // output_norm
+  if (!c.tied_head) plan_tiled(bufs, (uint64_t)P.Vl, d, [&](uint64_t j) { return j * d; });
+  const SessionSizes z = session_sizes(c, P.Hl, P.Hkvl, P.Fl, P.Vl, (int)context_length, sms);
+  const bool prompt_pass = c.tp_size == 1 && d % 256 == 0 && nq % 256 == 0 && fl % 256 == 0;
+  const PrefillSizes pz =
+      prefill_sizes(d, nq, fl, std::min<uint64_t>(context_length, (uint64_t)kPrefillChunk));
+  for (uint32_t i = 0; i < sessions; ++i) {
+    bufs.push_back({z.cache, kLedgerKv});
+    bufs.push_back({z.cache, kLedgerKv});
+    bufs.push_back({z.rope, kLedgerConcurrent});
+    for (int k = 0; k < 4; ++k) bufs.push_back({z.vec_d, kLedgerActivation});
+    for (int k = 0; k < 2; ++k) bufs.push_back({z.vec_q, kLedgerActivation});
+    for (uint64_t b : {z.hh, z.logits, z.logits_full, z.attn_part, z.attn_counters})
+      bufs.push_back({b, kLedgerActivation});
+    for (uint64_t b : {z.state, z.gen, z.prompt}) bufs.push_back({b, kLedgerConcurrent});
+    bufs.push_back({z.tp_buf, kLedgerStaging});
+    if (prompt_pass)
+      for (uint64_t b : {pz.h, pz.xs, pz.scale, pz.q, pz.ctx, pz.act}) bufs.push_back({b, kLedgerActivation});
+  }
+  uint64_t live[kLedgerClasses] = {};
+  for (const auto& b : bufs) {
+    if (b.first == 0) continue;
+    const uint64_t charged = ledger_charge(b.first);
+    FABER_ARG(charged != 0, "buffer size overflows the allocator policy");
+    live[b.second] += b.first;
+    live[kLedgerOverhead] += charged - b.first;
+  }
+  FaberPartitionLedgerV1 L;
+  L.weight_bytes = live[kLedgerWeights];
+  L.kv_cache_bytes = live[kLedgerKv];
+  L.activation_scratch_bytes = live[kLedgerActivation];
+  L.module_storage_bytes = static_attn_module_bytes();
+  L.allocator_overhead_bytes = live[kLedgerOverhead];
+  L.transfer_staging_bytes = live[kLedgerStaging];
+  L.concurrent_state_bytes = live[kLedgerConcurrent];
+  return L;
+}
+
 }  // namespace faber
 
 // ---------------------------------------------------------------------------
@@ -1643,6 +1780,16 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1*
       FABER_NCCL(ncclCommInitRank(&M.comm, M.tp, id, M.rank));
     }
     *out = m.release();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_partition_plan(const FaberModelConfigV1* cfg,
+                                                         uint32_t context_length, uint32_t sessions,
+                                                         int32_t sms, FaberPartitionLedgerV1* out) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_partition_plan", [&] {
+    FABER_ARG(cfg && out, "null pointer");
+    *out = partition_plan(*cfg, context_length, sessions, sms);
   });
 }
 

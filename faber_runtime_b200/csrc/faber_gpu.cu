@@ -134,29 +134,123 @@ void launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
 }
 
 // ---------------------------------------------------------------------------
+// Partition byte accounting: the classes of PartitionBudgetLedger
+// (src/partition.rs:111-137). Every device buffer is charged to one class of
+// the device it lives on when allocated and credited back when freed. The
+// allocator policy charges a buffer below 1 MiB in 512-byte units and a
+// larger one in 2 MiB units (the driver's suballocation and large-page
+// granularity); the rounding is the allocator-overhead class. With a policy
+// limit set, an allocation whose charge would take the device's total above
+// it fails before cudaMalloc runs. The tables are constant-initialized and
+// trivially destructible, so buffers freed during static destruction still
+// find them.
+// ---------------------------------------------------------------------------
+enum LedgerClass : int {
+  kLedgerWeights = 0,
+  kLedgerKv = 1,
+  kLedgerActivation = 2,
+  kLedgerModule = 3,
+  kLedgerOverhead = 4,
+  kLedgerStaging = 5,
+  kLedgerConcurrent = 6,
+  kLedgerClasses = 7
+};
+constexpr int kLedgerMaxDevices = 64;
+
+struct DeviceLedger {
+  uint64_t live[kLedgerClasses];
+  uint64_t limit;  // 0: no policy limit
+  bool touched;    // the device has held a buffer of this library
+};
+
+static std::mutex g_ledger_mu;
+static DeviceLedger g_ledger[kLedgerMaxDevices];
+
+// Class 4: the allocation-free attention scratch of the module image
+// (defined with that entry point), counted from a device's first buffer on.
+uint64_t static_attn_module_bytes();
+
+// The policy charge of an n-byte buffer (0 when it cannot be represented).
+inline uint64_t ledger_charge(uint64_t n) {
+  if (n == 0) return 0;
+  const uint64_t unit = n < (uint64_t(1) << 20) ? 512 : (uint64_t(2) << 20);
+  if (n > UINT64_MAX - unit) return 0;
+  return (n + unit - 1) / unit * unit;
+}
+
+inline uint64_t ledger_total(const DeviceLedger& L) {
+  uint64_t t = 0;
+  for (int c = 0; c < kLedgerClasses; ++c) t += L.live[c];
+  return t;
+}
+
+// Charges n bytes of class cls to device dev, or throws ALLOCATION when the
+// device's policy limit would be passed. Ordinals above the table are not
+// accounted (no limit applies there).
+inline void ledger_take(int dev, int cls, uint64_t n) {
+  if (dev < 0 || dev >= kLedgerMaxDevices || n == 0) return;
+  const uint64_t c = ledger_charge(n);
+  std::lock_guard<std::mutex> g(g_ledger_mu);
+  DeviceLedger& L = g_ledger[dev];
+  const uint64_t module = L.touched ? 0 : static_attn_module_bytes();
+  const uint64_t held = ledger_total(L) + module;
+  if (c == 0 || (L.limit && (c > L.limit || held > L.limit - c)))
+    throw Error(FABER_STATUS_ALLOCATION,
+                "partition budget: " + std::to_string(n) + " bytes (charged " + std::to_string(c) +
+                    ") on device " + std::to_string(dev) + " holding " + std::to_string(held) +
+                    " of a " + std::to_string(L.limit) + "-byte limit");
+  L.live[kLedgerModule] += module;
+  L.live[cls] += n;
+  L.live[kLedgerOverhead] += c - n;
+  L.touched = true;
+}
+
+inline void ledger_give(int dev, int cls, uint64_t n) {
+  if (dev < 0 || dev >= kLedgerMaxDevices || n == 0) return;
+  const uint64_t c = ledger_charge(n);
+  std::lock_guard<std::mutex> g(g_ledger_mu);
+  DeviceLedger& L = g_ledger[dev];
+  L.live[cls] -= n;
+  L.live[kLedgerOverhead] -= c - n;
+}
+
+// ---------------------------------------------------------------------------
 // Device buffers
 // ---------------------------------------------------------------------------
 struct DevBuf {
   void* p = nullptr;
   size_t n = 0;
   int dev = -1;
+  int cls = kLedgerActivation;
   DevBuf() = default;
-  explicit DevBuf(size_t bytes) { alloc(bytes); }
+  explicit DevBuf(size_t bytes, int ledger_class = kLedgerActivation) { alloc(bytes, ledger_class); }
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
-  DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n), dev(o.dev) { o.p = nullptr; o.n = 0; }
+  DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n), dev(o.dev), cls(o.cls) { o.p = nullptr; o.n = 0; }
   DevBuf& operator=(DevBuf&& o) noexcept {
-    if (this != &o) { release(); p = o.p; n = o.n; dev = o.dev; o.p = nullptr; o.n = 0; }
+    if (this != &o) {
+      release();
+      p = o.p;
+      n = o.n;
+      dev = o.dev;
+      cls = o.cls;
+      o.p = nullptr;
+      o.n = 0;
+    }
     return *this;
   }
   ~DevBuf() { release(); }
-  void alloc(size_t bytes) {
+  void alloc(size_t bytes, int ledger_class = kLedgerActivation) {
     release();
     FABER_CUDA(cudaGetDevice(&dev));
+    cls = ledger_class;
     if (bytes) {
+      ledger_take(dev, cls, bytes);  // a passed limit allocates nothing
       cudaError_t e = cudaMalloc(&p, bytes);
       if (e != cudaSuccess) {
         cudaGetLastError();
+        p = nullptr;
+        ledger_give(dev, cls, bytes);
         throw Error(FABER_STATUS_ALLOCATION, "cudaMalloc(" + std::to_string(bytes) + ") failed: " +
                                                  cudaGetErrorString(e));
       }
@@ -170,6 +264,7 @@ struct DevBuf {
       if (dev >= 0 && cur != dev) cudaSetDevice(dev);
       cudaFree(p);
       if (dev >= 0 && cur != dev && cur >= 0) cudaSetDevice(cur);
+      ledger_give(dev, cls, n);
     }
     p = nullptr;
     n = 0;
@@ -177,8 +272,8 @@ struct DevBuf {
   template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
-inline void upload(DevBuf& b, const void* host, size_t bytes) {
-  b.alloc(bytes);
+inline void upload(DevBuf& b, const void* host, size_t bytes, int ledger_class = kLedgerActivation) {
+  b.alloc(bytes, ledger_class);
   if (bytes) FABER_CUDA(cudaMemcpy(b.p, host, bytes, cudaMemcpyHostToDevice));
 }
 
@@ -189,7 +284,7 @@ struct DeviceTiled {
   bool identity = true;
   uint64_t hash = 0;
   void from(const TiledQ4k& T) {
-    upload(w, T.data.data(), T.data.size());
+    upload(w, T.data.data(), T.data.size(), kLedgerWeights);
     n_tiles = T.n_tiles;
     nb = T.nb;
     rows = T.rows;
@@ -197,8 +292,8 @@ struct DeviceTiled {
     identity = T.identity;
     hash = repack_hash(T);
     if (!identity) {
-      upload(xoff, T.xoff.data(), T.xoff.size() * sizeof(int32_t));
-      upload(rowmap, T.rowmap.data(), T.rowmap.size() * sizeof(int32_t));
+      upload(xoff, T.xoff.data(), T.xoff.size() * sizeof(int32_t), kLedgerWeights);
+      upload(rowmap, T.rowmap.data(), T.rowmap.size() * sizeof(int32_t), kLedgerWeights);
     } else {
       xoff.release();
       rowmap.release();
@@ -332,7 +427,7 @@ __attribute__((visibility("default"))) FaberRtStatusV1 __faber_gpu_v1_copy_in(
     FABER_ARG(!(data_len > 0 && data_ptr == nullptr), "null data pointer with nonzero length");
     std::lock_guard<std::mutex> lk(g_place_mu);
     DevBuf b;
-    upload(b, data_ptr, data_len);
+    upload(b, data_ptr, data_len, kLedgerConcurrent);  // host-keyed runtime state
     placed()[logical_id] = std::move(b);
   });
 }
@@ -576,6 +671,8 @@ constexpr int kStaticAttnMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_static_attn_scratch[kStaticAttnBytes];
 
+uint64_t static_attn_module_bytes() { return (uint64_t)kStaticAttnBytes; }
+
 // Argument check that builds its message only on failure (the shared
 // require() takes a std::string, which would allocate on every call).
 inline void static_check(bool cond, int code, const char* msg) {
@@ -795,6 +892,64 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_get_str
 
 __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_free(FaberGguf* g) {
   return guarded("faber_gpu_v2_gguf_free", [&] { delete g; });
+}
+
+// --- partition budget (src/partition.rs:111-155, 293-315) ------------------
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_partition_admit(
+    const FaberPartitionLedgerV1* declared, uint64_t safe_limit_bytes, uint64_t* total_out) {
+  return guarded("faber_gpu_v2_partition_admit", [&] {
+    FABER_ARG(declared != nullptr && total_out != nullptr, "null ledger or output");
+    const uint64_t cls[kLedgerClasses] = {
+        declared->weight_bytes,           declared->kv_cache_bytes,
+        declared->activation_scratch_bytes, declared->module_storage_bytes,
+        declared->allocator_overhead_bytes, declared->transfer_staging_bytes,
+        declared->concurrent_state_bytes};
+    // PartitionBudgetLedger::total_bytes: checked sum, overflow fails closed
+    uint64_t total = 0;
+    bool overflow = false;
+    for (uint64_t v : cls) {
+      if (v > UINT64_MAX - total) {
+        overflow = true;
+        break;
+      }
+      total += v;
+    }
+    *total_out = overflow ? UINT64_MAX : total;
+    require(!overflow, FABER_STATUS_BUDGET_EXCEEDED, "declared ledger overflows u64");
+    require(total <= safe_limit_bytes, FABER_STATUS_BUDGET_EXCEEDED,
+            "declared " + std::to_string(total) + " bytes exceed the " +
+                std::to_string(safe_limit_bytes) + "-byte safe limit");
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_partition_usage(
+    int32_t device, FaberPartitionLedgerV1* out) {
+  return guarded("faber_gpu_v2_partition_usage", [&] {
+    FABER_ARG(out != nullptr, "null output");
+    FABER_ARG(device >= 0 && device < kLedgerMaxDevices, "device ordinal outside 0-63");
+    std::lock_guard<std::mutex> g(g_ledger_mu);
+    const DeviceLedger& L = g_ledger[device];
+    out->weight_bytes = L.live[kLedgerWeights];
+    out->kv_cache_bytes = L.live[kLedgerKv];
+    out->activation_scratch_bytes = L.live[kLedgerActivation];
+    out->module_storage_bytes = L.live[kLedgerModule];
+    out->allocator_overhead_bytes = L.live[kLedgerOverhead];
+    out->transfer_staging_bytes = L.live[kLedgerStaging];
+    out->concurrent_state_bytes = L.live[kLedgerConcurrent];
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_partition_set_limit(
+    int32_t device, uint64_t safe_limit_bytes) {
+  return guarded("faber_gpu_v2_partition_set_limit", [&] {
+    FABER_ARG(device >= 0 && device < kLedgerMaxDevices, "device ordinal outside 0-63");
+    std::lock_guard<std::mutex> g(g_ledger_mu);
+    DeviceLedger& L = g_ledger[device];
+    const uint64_t held = ledger_total(L);
+    require(safe_limit_bytes == 0 || held <= safe_limit_bytes, FABER_STATUS_BUDGET_EXCEEDED,
+            "device " + std::to_string(device) + " already holds " + std::to_string(held) + " bytes");
+    L.limit = safe_limit_bytes;
+  });
 }
 
 }  // extern "C"

@@ -42,9 +42,13 @@ class DeviceModel:
         h = ctypes.c_void_p()
         _lib.call("faber_gpu_v2_model_create", ctypes.byref(c), ctypes.byref(h))
         self._h = h
-        for name, gtype, arr, rows, cols in tensors:
-            self.set_tensor(name, gtype, arr, rows, cols)
-        _lib.call("faber_gpu_v2_model_finalize", self._h)
+        try:
+            for name, gtype, arr, rows, cols in tensors:
+                self.set_tensor(name, gtype, arr, rows, cols)
+            _lib.call("faber_gpu_v2_model_finalize", self._h)
+        except BaseException:
+            self.close()  # a failed upload frees what it had placed on the device
+            raise
 
     def set_tensor(self, name: str, gtype: int, arr: np.ndarray, rows: int, cols: int) -> None:
         a = np.ascontiguousarray(arr)

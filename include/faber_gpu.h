@@ -41,7 +41,10 @@ enum {
   FABER_STATUS_CANCELLED = 18,
   FABER_STATUS_ALLOCATION = 19,
   FABER_STATUS_CUDA_ERROR = 20,
-  FABER_STATUS_KERNEL_ERROR = 21
+  FABER_STATUS_KERNEL_ERROR = 21,
+  /* admission refused: the declared ledger exceeds the partition's safe
+   * limit (AdmissionError::BudgetExceeded, src/partition.rs:236-247) */
+  FABER_STATUS_BUDGET_EXCEEDED = 22
 };
 
 /* GGUF dtype ids of the admitted tensor types (src/gguf.rs:135-144). */
@@ -212,6 +215,56 @@ typedef struct FaberKvLayoutV1 {
  * INVALID_ARGUMENT (KvCacheLayout::new returns None), overflow is IO_ERROR. */
 FaberRtStatusV1 faber_gpu_v2_kv_layout_bytes(const FaberKvLayoutV1* layout, uint64_t* total,
                                              uint64_t* admitted);
+
+/* One partition's device bytes by class: PartitionBudgetLedger
+ * (src/partition.rs:111-155), classes 1-7 in field order; class 8 of the
+ * reference's admission equation is the safe limit passed beside it. */
+typedef struct FaberPartitionLedgerV1 {
+  uint64_t weight_bytes;             /* 1: weights, including repack */
+  uint64_t kv_cache_bytes;           /* 2: KV cache */
+  uint64_t activation_scratch_bytes; /* 3: activations and operation scratch */
+  uint64_t module_storage_bytes;     /* 4: module-resident device storage */
+  uint64_t allocator_overhead_bytes; /* 5: allocator granularity */
+  uint64_t transfer_staging_bytes;   /* 6: exchange and staging buffers */
+  uint64_t concurrent_state_bytes;   /* 7: per-request state (tokens, positions) */
+} FaberPartitionLedgerV1;
+
+/* Admission of a declared ledger against a policy limit
+ * (VirtualDevicePartition::admit, src/partition.rs:293-315): OK when the
+ * checked sum of the seven classes is at most safe_limit_bytes, else
+ * BUDGET_EXCEEDED, also when the sum overflows (then *total_out is
+ * UINT64_MAX). Arithmetic only: nothing is allocated, no device is needed. */
+FaberRtStatusV1 faber_gpu_v2_partition_admit(const FaberPartitionLedgerV1* declared,
+                                             uint64_t safe_limit_bytes, uint64_t* total_out);
+
+/* The bytes this library holds on a device, by class. Every device buffer is
+ * charged to one class when it is allocated and credited back when freed.
+ * Class 5 is this library's allocator policy: a buffer below 1 MiB is
+ * charged in 512-byte units and a larger one in 2 MiB units, and the
+ * rounding is class 5. Class 4 is the allocation-free attention scratch of
+ * the module image, counted once the device holds any buffer. Arithmetic on
+ * host counters only (no device call). Device ordinals 0-63. */
+FaberRtStatusV1 faber_gpu_v2_partition_usage(int32_t device, FaberPartitionLedgerV1* out);
+
+/* Sets a device's policy limit in bytes (0 removes it). While a limit is
+ * set, an allocation whose charge would take the device's total (classes
+ * 1-7) above it fails with ALLOCATION before cudaMalloc runs: growth after
+ * admission is an allocation outcome, never a ledger rewrite
+ * (src/partition.rs:111-114). A limit below what the device already holds
+ * is BUDGET_EXCEEDED and leaves the previous limit in place. */
+FaberRtStatusV1 faber_gpu_v2_partition_set_limit(int32_t device, uint64_t safe_limit_bytes);
+
+/* The ledger of one tensor-parallel rank (cfg->tp_size, cfg->tp_rank) before
+ * anything is allocated, for the admission check: the model's Q4_K linears
+ * in their tiled layout, the f16 embedding and the norms, then `sessions`
+ * sessions of context_length positions (KV cache, step buffers, and the
+ * prompt pass's scratch where that pass runs), with the attention split
+ * count of a device with `sms` SMs. Every buffer is charged by the allocator
+ * policy of faber_gpu_v2_partition_usage, so a model and its sessions built
+ * from Q4_K tensors hold exactly this ledger. Host-only. */
+FaberRtStatusV1 faber_gpu_v2_partition_plan(const FaberModelConfigV1* cfg, uint32_t context_length,
+                                            uint32_t sessions, int32_t sms,
+                                            FaberPartitionLedgerV1* out);
 
 FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1* cfg, FaberGpuModel** out);
 /* Upload one tensor by its GGUF name (token_embd.weight, output_norm.weight,
