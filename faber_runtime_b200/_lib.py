@@ -50,6 +50,39 @@ class PartitionLedgerC(ctypes.Structure):
                 ("concurrent_state_bytes", ctypes.c_uint64)]
 
 
+class TxnOpC(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_uint32), ("partition", ctypes.c_uint32), ("destination", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32), ("participants", ctypes.c_uint64), ("ref", ctypes.c_uint64),
+                ("bytes", ctypes.c_uint64)]
+
+
+class TxnPartitionC(ctypes.Structure):
+    _fields_ = [("partition", ctypes.c_uint32), ("admitted", ctypes.c_uint32), ("ledger", PartitionLedgerC)]
+
+
+class TxnReceiptC(ctypes.Structure):
+    _fields_ = [("decision", ctypes.c_int32), ("state", ctypes.c_int32), ("failure_kind", ctypes.c_int32),
+                ("failure_class", ctypes.c_int32), ("failure_partition", ctypes.c_uint32),
+                ("published", ctypes.c_uint32), ("publication_ordinal", ctypes.c_uint64),
+                ("declared_write_bytes", ctypes.c_uint64), ("executed_operations", ctypes.c_uint64),
+                ("executed_bytes", ctypes.c_uint64), ("completed_events", ctypes.c_uint64),
+                ("staged_bytes", ctypes.c_uint64), ("published_bytes", ctypes.c_uint64),
+                ("released_partitions", ctypes.c_uint64), ("retired_partitions", ctypes.c_uint64),
+                ("partial_publication", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+                ("prepare_ns", ctypes.c_uint64), ("execute_ns", ctypes.c_uint64), ("finalize_ns", ctypes.c_uint64)]
+
+
+class TxnErrorC(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("partition", ctypes.c_uint32), ("backend_class", ctypes.c_int32),
+                ("budget_class", ctypes.c_int32), ("missing", ctypes.c_uint64)]
+
+
+class TxnBackendInfoC(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "reserved_partitions", "released_partitions", "retired_partitions", "staged_bytes", "published_bytes",
+        "committed_bytes", "executed_operations", "pending_events", "delivered_faults", "reclaimed_copy_bytes")]
+
+
 class FaberError(RuntimeError):
     """A failed C-ABI call: ``code`` is the FaberRtStatusV1 code."""
 
@@ -91,6 +124,25 @@ SIGNATURES = {
     "faber_gpu_v2_partition_set_limit": (Status, [I32, U64]),
     "faber_gpu_v2_partition_plan": (Status, [ctypes.POINTER(ModelConfigC), U32, U32, I32,
                                              ctypes.POINTER(PartitionLedgerC)]),
+    "faber_gpu_v2_txn_create": (Status, [P, U32, P, U32, P, U32, P, U32, PP]),
+    "faber_gpu_v2_txn_prepare": (Status, [P, P]),
+    "faber_gpu_v2_txn_execute": (Status, [P, P]),
+    "faber_gpu_v2_txn_execute_operation": (Status, [P, P, P]),
+    "faber_gpu_v2_txn_commit": (Status, [P, P, U64]),
+    "faber_gpu_v2_txn_abort": (Status, [P, P, ctypes.c_char_p]),
+    "faber_gpu_v2_txn_receipt": (Status, [P, P]),
+    "faber_gpu_v2_txn_last_error": (Status, [P, P]),
+    "faber_gpu_v2_txn_reservation": (Status, [P, U32, P]),
+    "faber_gpu_v2_txn_free": (Status, [P]),
+    "faber_gpu_v2_txn_backend_fake": (Status, [PP]),
+    "faber_gpu_v2_txn_backend_inject": (Status, [P, U32, U64, U32, I32]),
+    "faber_gpu_v2_txn_backend_fail_publish": (Status, [P, I32]),
+    "faber_gpu_v2_txn_backend_set_auto_complete": (Status, [P, I32]),
+    "faber_gpu_v2_txn_backend_complete_event": (Status, [P, U32, U32, U64]),
+    "faber_gpu_v2_txn_backend_info": (Status, [P, P]),
+    "faber_gpu_v2_txn_backend_free": (Status, [P]),
+    "faber_gpu_v2_tp_step_plan": (Status, [ctypes.POINTER(ModelConfigC), U32, P, U32, ctypes.POINTER(U32),
+                                           ctypes.POINTER(U64), P]),
     "faber_gpu_v2_model_create": (Status, [ctypes.POINTER(ModelConfigC), PP]),
     "faber_gpu_v2_model_set_tensor": (Status, [P, ctypes.c_char_p, U32, P, U64, U64, U64]),
     "faber_gpu_v2_tp_shard": (Status, [ctypes.POINTER(ModelConfigC), ctypes.c_char_p, P]),

@@ -1654,6 +1654,42 @@ inline void set_prefix(SessionState& S, uint32_t layer, const float* k, const fl
   FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
 }
 
+// One decode step of a tensor-parallel group as a transaction plan
+// (src/execution_transaction/transaction.rs over the group's ranks): a
+// launch per rank, whose published output is the position's K/V rows of
+// its kv heads (f16) and the token, then a barrier over all ranks: the
+// step's exchanges. The O and down partials cross through each rank's
+// exchange buffer and are consumed inside the step, so they publish
+// nothing; that buffer is admitted with the session (class 6). A rank whose
+// exchange fails is a fault of the barrier on that rank. The commit
+// boundary is the barrier and every launch. References: position << 16 |
+// tag << 8 | rank (tag 1 launch, 3 barrier).
+inline void tp_step_plan(const FaberModelConfigV1& c, uint32_t position, std::vector<FaberTxnOpV1>& ops,
+                         uint64_t& barrier_ref, std::vector<uint64_t>& launch_refs) {
+  validate_config(c);
+  FABER_ARG(c.tp_size >= 2, "a single rank runs no group transaction");
+  const uint64_t tp = c.tp_size, hd = c.head_dim;
+  const uint64_t kv_rows = (uint64_t)c.n_layers * (c.n_kv_heads / tp) * hd * 2 * 2;
+  const uint64_t base = (uint64_t)position << 16;
+  ops.clear();
+  launch_refs.clear();
+  for (uint32_t r = 0; r < tp; ++r) {
+    FaberTxnOpV1 op{};
+    op.kind = FABER_TXN_LAUNCH;
+    op.partition = r;
+    op.ref = base | 1u << 8 | r;
+    op.bytes = kv_rows + 8;
+    ops.push_back(op);
+    launch_refs.push_back(op.ref);
+  }
+  FaberTxnOpV1 op{};
+  op.kind = FABER_TXN_BARRIER;
+  op.participants = tp >= 64 ? ~0ull : (1ull << tp) - 1;
+  op.ref = base | 3u << 8;
+  ops.push_back(op);
+  barrier_ref = op.ref;
+}
+
 // The device buffers of a tiled Q4_K linear whose row j starts at element
 // start(j) of its source: repack_q4k groups rows by their offset inside a
 // super-block, 16 rows per tile, and keeps a tile offset and row map unless
@@ -1790,6 +1826,25 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_partition_plan(const FaberModelConfigV
   return guarded("faber_gpu_v2_partition_plan", [&] {
     FABER_ARG(cfg && out, "null pointer");
     *out = partition_plan(*cfg, context_length, sessions, sms);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_tp_step_plan(const FaberModelConfigV1* cfg, uint32_t position,
+                                                       FaberTxnOpV1* ops, uint32_t cap, uint32_t* n_ops,
+                                                       uint64_t* boundary_barrier, uint64_t* boundary_launches) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_tp_step_plan", [&] {
+    FABER_ARG(cfg && n_ops && boundary_barrier, "null pointer");
+    std::vector<FaberTxnOpV1> v;
+    std::vector<uint64_t> launches;
+    uint64_t barrier = 0;
+    tp_step_plan(*cfg, position, v, barrier, launches);
+    *n_ops = (uint32_t)v.size();
+    require(ops != nullptr && boundary_launches != nullptr && cap >= v.size(), FABER_STATUS_IO_ERROR,
+            "plan needs " + std::to_string(v.size()) + " operations");
+    std::copy(v.begin(), v.end(), ops);
+    std::copy(launches.begin(), launches.end(), boundary_launches);
+    *boundary_barrier = barrier;
   });
 }
 

@@ -18,6 +18,7 @@
 #include "gguf.hpp"
 #include "ops.cuh"
 #include "repack.hpp"
+#include "transaction.hpp"
 
 namespace faber {
 
@@ -892,6 +893,231 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_get_str
 
 __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_free(FaberGguf* g) {
   return guarded("faber_gpu_v2_gguf_free", [&] { delete g; });
+}
+
+// --- execution transaction (src/execution_transaction/transaction.rs) ------
+struct FaberTxn {
+  faber::txn::Transaction t;
+  faber::txn::Outcome last;
+};
+
+struct FaberTxnBackend {
+  faber::txn::FaultBackend b;
+};
+
+namespace {
+
+faber::txn::Op txn_op(const FaberTxnOpV1& o) {
+  FABER_ARG(o.kind <= FABER_TXN_BARRIER, "unknown operation kind " + std::to_string(o.kind));
+  FABER_ARG(o.partition < 64 && o.destination < 64, "partition ordinal above 63");
+  faber::txn::Op op;
+  op.kind = (faber::txn::OpKind)o.kind;
+  op.partition = o.partition;
+  op.destination = o.kind == FABER_TXN_TRANSFER ? o.destination : 0;
+  op.participants = (o.kind == FABER_TXN_BROADCAST || o.kind == FABER_TXN_BARRIER) ? o.participants : 0;
+  op.ref = o.ref;
+  op.bytes = o.kind == FABER_TXN_BARRIER ? 0 : o.bytes;
+  if (o.kind == FABER_TXN_BROADCAST)
+    FABER_ARG(o.participants >> o.partition & 1, "a broadcast's source must participate");
+  if (o.kind == FABER_TXN_BARRIER) FABER_ARG(o.participants != 0, "a barrier needs participants");
+  return op;
+}
+
+// Records a lifecycle outcome on the transaction and turns a failure into
+// its status code.
+void txn_finish(FaberTxn* t, const faber::txn::Outcome& o) {
+  using namespace faber::txn;
+  t->last = o;
+  if (o.ok()) return;
+  int code = FABER_STATUS_INVALID_ARGUMENT;
+  if (o.kind == kTxnReservationExceedsBudget) code = FABER_STATUS_BUDGET_EXCEEDED;
+  if (o.kind == kTxnBoundaryNotReached) code = FABER_STATUS_FALLIBLE;
+  if (o.kind == kTxnBackend || o.kind == kTxnPublishFailed) {
+    switch (o.backend.cls) {
+      case ErrClass::Allocation: code = FABER_STATUS_ALLOCATION; break;
+      case ErrClass::Operation: code = FABER_STATUS_KERNEL_ERROR; break;
+      case ErrClass::DeviceLoss: code = FABER_STATUS_DEVICE_LOSS; break;
+      case ErrClass::Cancelled: code = FABER_STATUS_CANCELLED; break;
+      case ErrClass::Timeout: code = FABER_STATUS_TIMEOUT; break;
+    }
+  }
+  throw Error(code, o.message);
+}
+
+}  // namespace
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_create(
+    const FaberTxnPartitionV1* partitions, uint32_t n_partitions, const FaberTxnOpV1* ops, uint32_t n_ops,
+    const uint64_t* boundary_barriers, uint32_t n_barriers, const uint64_t* boundary_launches,
+    uint32_t n_launches, FaberTxn** out) {
+  return guarded("faber_gpu_v2_txn_create", [&] {
+    FABER_ARG(out != nullptr, "null output");
+    *out = nullptr;
+    FABER_ARG((partitions || !n_partitions) && (ops || !n_ops) && (boundary_barriers || !n_barriers) &&
+                  (boundary_launches || !n_launches),
+              "null array with a nonzero count");
+    std::map<uint32_t, faber::txn::BoundPartition> plan;
+    for (uint32_t i = 0; i < n_partitions; ++i) {
+      FABER_ARG(partitions[i].partition < 64, "partition ordinal above 63");
+      FABER_ARG(!plan.count(partitions[i].partition), "partition bound twice");
+      plan[partitions[i].partition] = {partitions[i].admitted != 0, partitions[i].ledger};
+    }
+    std::vector<faber::txn::Op> v;
+    for (uint32_t i = 0; i < n_ops; ++i) v.push_back(txn_op(ops[i]));
+    auto t = std::make_unique<FaberTxn>();
+    const faber::txn::Outcome o = faber::txn::Transaction::create(
+        std::move(plan), std::move(v), std::vector<uint64_t>(boundary_barriers, boundary_barriers + n_barriers),
+        std::vector<uint64_t>(boundary_launches, boundary_launches + n_launches), t->t);
+    if (!o.ok()) throw Error(FABER_STATUS_INVALID_ARGUMENT, o.message);
+    *out = t.release();
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_prepare(FaberTxn* t, FaberTxnBackend* b) {
+  return guarded("faber_gpu_v2_txn_prepare", [&] {
+    FABER_ARG(t && b, "null pointer");
+    txn_finish(t, t->t.prepare(b->b));
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_execute(FaberTxn* t, FaberTxnBackend* b) {
+  return guarded("faber_gpu_v2_txn_execute", [&] {
+    FABER_ARG(t && b, "null pointer");
+    txn_finish(t, t->t.execute(b->b));
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_execute_operation(
+    FaberTxn* t, FaberTxnBackend* b, const FaberTxnOpV1* op) {
+  return guarded("faber_gpu_v2_txn_execute_operation", [&] {
+    FABER_ARG(t && b && op, "null pointer");
+    txn_finish(t, t->t.execute_operation(b->b, txn_op(*op)));
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_commit(FaberTxn* t, FaberTxnBackend* b,
+                                                                               uint64_t publication_ordinal) {
+  return guarded("faber_gpu_v2_txn_commit", [&] {
+    FABER_ARG(t && b, "null pointer");
+    txn_finish(t, t->t.commit(b->b, publication_ordinal));
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_abort(FaberTxn* t, FaberTxnBackend* b,
+                                                                              const char* reason) {
+  return guarded("faber_gpu_v2_txn_abort", [&] {
+    FABER_ARG(t && b, "null pointer");
+    txn_finish(t, t->t.abort(b->b, reason ? reason : ""));
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_receipt(const FaberTxn* t,
+                                                                                FaberTxnReceiptV1* out) {
+  return guarded("faber_gpu_v2_txn_receipt", [&] {
+    FABER_ARG(t && out, "null pointer");
+    t->t.receipt(*out);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_last_error(const FaberTxn* t,
+                                                                                   FaberTxnErrorV1* out) {
+  return guarded("faber_gpu_v2_txn_last_error", [&] {
+    FABER_ARG(t && out, "null pointer");
+    const bool be = t->last.kind == faber::txn::kTxnBackend || t->last.kind == faber::txn::kTxnPublishFailed;
+    out->kind = t->last.kind;
+    out->partition = t->last.partition;
+    out->backend_class = be ? (int32_t)t->last.backend.cls : 0;
+    out->budget_class = t->last.budget_class;
+    out->missing = t->last.missing;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_reservation(const FaberTxn* t,
+                                                                                    uint32_t partition,
+                                                                                    uint64_t out[4]) {
+  return guarded("faber_gpu_v2_txn_reservation", [&] {
+    FABER_ARG(t && out, "null pointer");
+    const auto& r = t->t.reservation();
+    auto it = r.find(partition);
+    FABER_ARG(it != r.end(), "no reservation for partition " + std::to_string(partition));
+    out[0] = it->second.staging;
+    out[1] = it->second.output;
+    out[2] = it->second.events;
+    out[3] = it->second.scratch;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_free(FaberTxn* t) {
+  return guarded("faber_gpu_v2_txn_free", [&] { delete t; });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_fake(FaberTxnBackend** out) {
+  return guarded("faber_gpu_v2_txn_backend_fake", [&] {
+    FABER_ARG(out != nullptr, "null output");
+    *out = new FaberTxnBackend();
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_inject(
+    FaberTxnBackend* b, uint32_t op_kind, uint64_t ref, uint32_t partition, int32_t fault_class) {
+  return guarded("faber_gpu_v2_txn_backend_inject", [&] {
+    FABER_ARG(b != nullptr, "null backend");
+    FABER_ARG(op_kind <= FABER_TXN_BARRIER && partition < 64, "bad operation kind or partition");
+    FABER_ARG(fault_class >= 1 && fault_class <= 5, "fault class must be 1-5");
+    b->b.faults.push_back({{op_kind, ref}, partition, (faber::txn::FaultClass)fault_class});
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_fail_publish(
+    FaberTxnBackend* b, int32_t backend_class) {
+  return guarded("faber_gpu_v2_txn_backend_fail_publish", [&] {
+    FABER_ARG(b != nullptr, "null backend");
+    FABER_ARG(backend_class >= 1 && backend_class <= 5, "backend error class must be 1-5");
+    b->b.fail_publish = (faber::txn::ErrClass)backend_class;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_set_auto_complete(
+    FaberTxnBackend* b, int32_t on) {
+  return guarded("faber_gpu_v2_txn_backend_set_auto_complete", [&] {
+    FABER_ARG(b != nullptr, "null backend");
+    b->b.inner.auto_complete = on != 0;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_complete_event(
+    FaberTxnBackend* b, uint32_t op_kind, uint32_t partition, uint64_t ref) {
+  return guarded("faber_gpu_v2_txn_backend_complete_event", [&] {
+    FABER_ARG(b != nullptr, "null backend");
+    FABER_ARG(op_kind <= FABER_TXN_BARRIER && partition < 64, "bad operation kind or partition");
+    b->b.inner.complete_event({op_kind, partition, ref});
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_info(const FaberTxnBackend* b,
+                                                                                     FaberTxnBackendInfoV1* out) {
+  return guarded("faber_gpu_v2_txn_backend_info", [&] {
+    FABER_ARG(b && out, "null pointer");
+    const auto& in = b->b.inner;
+    *out = FaberTxnBackendInfoV1{};
+    for (const auto& kv : in.reservations) out->reserved_partitions |= 1ull << kv.first;
+    for (uint32_t p : in.released) out->released_partitions |= 1ull << p;
+    for (uint32_t p : in.retired) out->retired_partitions |= 1ull << p;
+    out->staged_bytes = in.staged_total;
+    out->published_bytes = in.published_total;
+    out->committed_bytes = b->b.committed_total;
+    out->executed_operations = in.executed.size();
+    uint64_t pending = 0;
+    for (const auto& e : in.dispatched)
+      if (!in.completed.count(e)) ++pending;
+    out->pending_events = pending;
+    out->delivered_faults = b->b.delivered.size();
+    for (const auto& d : b->b.delivered) out->reclaimed_copy_bytes += d.reclaimed_copy_bytes;
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_txn_backend_free(FaberTxnBackend* b) {
+  return guarded("faber_gpu_v2_txn_backend_free", [&] { delete b; });
 }
 
 // --- partition budget (src/partition.rs:111-155, 293-315) ------------------

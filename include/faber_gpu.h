@@ -266,6 +266,144 @@ FaberRtStatusV1 faber_gpu_v2_partition_plan(const FaberModelConfigV1* cfg, uint3
                                             uint32_t sessions, int32_t sms,
                                             FaberPartitionLedgerV1* out);
 
+/* --- execution transaction (src/execution_transaction/transaction.rs) ------
+ * prepare / execute / commit / abort of an operation plan over the ranks of
+ * a group (partitions 0-63). Lifecycle calls return OK, INVALID_ARGUMENT for
+ * a contract violation (wrong state, unknown partition, duplicate or
+ * undeclared operation, missing admitted budget, an operation outside the
+ * accepted snapshot, abort after commit), BUDGET_EXCEEDED when a
+ * reservation exceeds an admitted class, FALLIBLE when commit finds the
+ * boundary not yet reached (nothing published; commit may be called
+ * again), and for a backend failure the code of its class: ALLOCATION,
+ * KERNEL_ERROR (an operation or transfer error), DEVICE_LOSS, CANCELLED or
+ * TIMEOUT. faber_gpu_v2_txn_last_error gives the error's kind. */
+typedef struct FaberTxn FaberTxn;
+typedef struct FaberTxnBackend FaberTxnBackend;
+
+enum { FABER_TXN_LAUNCH = 0, FABER_TXN_TRANSFER = 1, FABER_TXN_BROADCAST = 2, FABER_TXN_BARRIER = 3 };
+
+/* One operation (TransactionOperation, mirror.rs:635-656); identity is
+ * (kind, ref). launch: partition, bytes = output bytes; transfer: partition
+ * = source, destination, bytes; broadcast: partition = source, participants
+ * mask, bytes; barrier: participants mask. */
+typedef struct FaberTxnOpV1 {
+  uint32_t kind;
+  uint32_t partition;
+  uint32_t destination;
+  uint32_t reserved;
+  uint64_t participants;
+  uint64_t ref;
+  uint64_t bytes;
+} FaberTxnOpV1;
+
+/* A partition of the bound plan and its admitted ledger (admitted = 0: none,
+ * which prepare refuses for a partition an operation uses). */
+typedef struct FaberTxnPartitionV1 {
+  uint32_t partition;
+  uint32_t admitted;
+  FaberPartitionLedgerV1 ledger;
+} FaberTxnPartitionV1;
+
+/* TransactionReceipt figures (receipt.rs). decision 0 none, 1 committed,
+ * 2 aborted; state 0 New, 1 Prepared, 2 Executing, 3 Committed, 4 Failed,
+ * 5 Aborted; failure_kind 0 none, 1 backend, 2 publish failed, 3 cancelled;
+ * failure_class 1 allocation, 2 operation, 3 device loss, 4 cancelled,
+ * 5 timeout. Partition sets are masks. */
+typedef struct FaberTxnReceiptV1 {
+  int32_t decision;
+  int32_t state;
+  int32_t failure_kind;
+  int32_t failure_class;
+  uint32_t failure_partition;
+  uint32_t published;
+  uint64_t publication_ordinal;
+  uint64_t declared_write_bytes;
+  uint64_t executed_operations;
+  uint64_t executed_bytes;
+  uint64_t completed_events;
+  uint64_t staged_bytes;
+  uint64_t published_bytes;
+  uint64_t released_partitions;
+  uint64_t retired_partitions;
+  uint32_t partial_publication;
+  uint32_t reserved;
+  uint64_t prepare_ns;
+  uint64_t execute_ns;
+  uint64_t finalize_ns;
+} FaberTxnReceiptV1;
+
+/* The last lifecycle error (errors.rs): kind 0 none, 1 DegeneratePlan,
+ * 2 EmptySnapshot, 3 InvalidState, 4 UnknownPartition, 5 DuplicateOperation,
+ * 6 UndeclaredBoundaryBarrier, 7 UndeclaredBoundaryLaunch,
+ * 8 MissingAdmittedBudget, 9 ReservationExceedsBudget (budget_class 6 or 3),
+ * 10 Backend, 11 OperationOutsideSnapshot, 12 BoundaryNotReached (missing =
+ * boundary refs pending), 13 PublishFailed, 14 AlreadyCommitted. */
+typedef struct FaberTxnErrorV1 {
+  int32_t kind;
+  uint32_t partition;
+  int32_t backend_class;
+  int32_t budget_class;
+  uint64_t missing;
+} FaberTxnErrorV1;
+
+/* ExecutionTransaction::new: INVALID_ARGUMENT for fewer than two partitions
+ * (DegeneratePlan) or no operations (EmptySnapshot). */
+FaberRtStatusV1 faber_gpu_v2_txn_create(const FaberTxnPartitionV1* partitions, uint32_t n_partitions,
+                                        const FaberTxnOpV1* ops, uint32_t n_ops,
+                                        const uint64_t* boundary_barriers, uint32_t n_barriers,
+                                        const uint64_t* boundary_launches, uint32_t n_launches,
+                                        FaberTxn** out);
+FaberRtStatusV1 faber_gpu_v2_txn_prepare(FaberTxn* t, FaberTxnBackend* b);
+FaberRtStatusV1 faber_gpu_v2_txn_execute(FaberTxn* t, FaberTxnBackend* b);
+FaberRtStatusV1 faber_gpu_v2_txn_execute_operation(FaberTxn* t, FaberTxnBackend* b, const FaberTxnOpV1* op);
+FaberRtStatusV1 faber_gpu_v2_txn_commit(FaberTxn* t, FaberTxnBackend* b, uint64_t publication_ordinal);
+FaberRtStatusV1 faber_gpu_v2_txn_abort(FaberTxn* t, FaberTxnBackend* b, const char* reason);
+FaberRtStatusV1 faber_gpu_v2_txn_receipt(const FaberTxn* t, FaberTxnReceiptV1* out);
+FaberRtStatusV1 faber_gpu_v2_txn_last_error(const FaberTxn* t, FaberTxnErrorV1* out);
+/* Reservation held for a partition after prepare: staging (class 6),
+ * output, event and scratch bytes (class 3). */
+FaberRtStatusV1 faber_gpu_v2_txn_reservation(const FaberTxn* t, uint32_t partition, uint64_t out[4]);
+FaberRtStatusV1 faber_gpu_v2_txn_free(FaberTxn* t);
+
+/* The fault-injecting host backend (src/fake_device.rs:184-318): the
+ * happy-path fake plus one-shot faults per (operation, partition). Fault
+ * classes: 1 cancel, 2 timeout, 3 transfer error, 4 kernel error, 5 device
+ * loss. Injection is on the host; no device is touched. */
+typedef struct FaberTxnBackendInfoV1 {
+  uint64_t reserved_partitions; /* mask of partitions holding a reservation */
+  uint64_t released_partitions;
+  uint64_t retired_partitions;
+  uint64_t staged_bytes;
+  uint64_t published_bytes;
+  uint64_t committed_bytes; /* the last successful publication */
+  uint64_t executed_operations;
+  uint64_t pending_events; /* dispatched, not yet completed */
+  uint64_t delivered_faults;
+  uint64_t reclaimed_copy_bytes;
+} FaberTxnBackendInfoV1;
+
+FaberRtStatusV1 faber_gpu_v2_txn_backend_fake(FaberTxnBackend** out);
+FaberRtStatusV1 faber_gpu_v2_txn_backend_inject(FaberTxnBackend* b, uint32_t op_kind, uint64_t ref,
+                                                uint32_t partition, int32_t fault_class);
+FaberRtStatusV1 faber_gpu_v2_txn_backend_fail_publish(FaberTxnBackend* b, int32_t backend_class);
+FaberRtStatusV1 faber_gpu_v2_txn_backend_set_auto_complete(FaberTxnBackend* b, int32_t on);
+FaberRtStatusV1 faber_gpu_v2_txn_backend_complete_event(FaberTxnBackend* b, uint32_t op_kind,
+                                                        uint32_t partition, uint64_t ref);
+FaberRtStatusV1 faber_gpu_v2_txn_backend_info(const FaberTxnBackend* b, FaberTxnBackendInfoV1* out);
+FaberRtStatusV1 faber_gpu_v2_txn_backend_free(FaberTxnBackend* b);
+
+/* One decode step of the tensor-parallel group cfg->tp_size (>= 2) as a
+ * transaction plan over its ranks: per rank a launch (its step; published
+ * output the position's K/V rows of its kv heads and the token), then a
+ * barrier over all ranks (the step's exchanges, whose partials are consumed
+ * inside the step through the session's exchange buffer). The commit
+ * boundary is the barrier and the tp_size launches.
+ * *n_ops is always set; with cap below it the call is IO_ERROR and writes
+ * nothing else. boundary_launches holds tp_size references. Host-only. */
+FaberRtStatusV1 faber_gpu_v2_tp_step_plan(const FaberModelConfigV1* cfg, uint32_t position,
+                                          FaberTxnOpV1* ops, uint32_t cap, uint32_t* n_ops,
+                                          uint64_t* boundary_barrier, uint64_t* boundary_launches);
+
 FaberRtStatusV1 faber_gpu_v2_model_create(const FaberModelConfigV1* cfg, FaberGpuModel** out);
 /* Upload one tensor by its GGUF name (token_embd.weight, output_norm.weight,
  * output.weight, blk.N.{attn_norm,attn_q,attn_k,attn_v,attn_output,ffn_norm,
