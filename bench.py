@@ -28,7 +28,9 @@ decode_batch16   sixteen sessions with their own prompts decoding K greedy
            aggregate tokens/s). --no-batch skips both legs.
 cpu_baseline  the C++ oracle restatement of the reference's CPU path on
            this host's cores: a 2-layer sample of the same model at
-           context 2048, extrapolated to 32 layers.
+           context 2048, extrapolated to 32 layers; beside it the same on
+           one thread (the reference's execution model) and the 4096 x 4096
+           Q4_K GEMV per call on all cores and on one.
 
 --impl reference times that CPU path as its own line (the reference is
 Rust with no toolchain here; its restatement is the oracle port).
@@ -237,11 +239,34 @@ def cpu_sample(cfg, threads=None):
     push = float(np.median([a for a, _ in times]))
     head = float(np.median([b for _, b in times]))
     per_token = push * cfg.n_layers / 2 + head
+    # one thread, the reference's own execution model: one more token
+    oracle.set_threads(1)
+    t0 = time.perf_counter()
+    run.push_token(tok)
+    t1 = time.perf_counter()
+    run.position_logits()
+    t2 = time.perf_counter()
+    per_token_1 = (t1 - t0) * cfg.n_layers / 2 + (t2 - t1)
+    # the 4096 x 4096 Q4_K GEMV (dequant fused, no materialization) per call
+    w = synth.q4k_blocks(SEED, 77, 4096 * 4096 // 256)
+    x = synth.normal(SEED, 78, 4096)
+    gemv_ms = {}
+    for n in (threads, 1):
+        oracle.set_threads(n)
+        reps, g0 = 0, time.perf_counter()
+        while reps < 3 or (time.perf_counter() - g0 < 0.5 and reps < 50):
+            oracle.dense_q(oracle.Q4_K, w, x, 4096, 4096)
+            reps += 1
+        gemv_ms[n] = (time.perf_counter() - g0) / reps * 1e3
+    oracle.set_threads(threads)
     return {"value": 1.0 / per_token, "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": f"C++ oracle, {cfg.name} cut to 2 of {cfg.n_layers} layers at context {PREFILL}, "
                       f"{len(times)} tokens (push {push:.3f} s + logits {head:.3f} s), per-token time "
                       f"extrapolated as push*{cfg.n_layers // 2} + logits",
-            "per_token_s": per_token}
+            "per_token_s": per_token,
+            "single_thread": {"value": 1.0 / per_token_1, "unit": "tok/s", "cores": 1,
+                              "sample": "one token of the same sample on one thread, extrapolated alike"},
+            "gemv_4096x4096_ms": {"cores": threads, "value": gemv_ms[threads], "single_thread": gemv_ms[1]}}
 
 
 def run_reference(args):
