@@ -83,12 +83,24 @@ class TxnBackendInfoC(ctypes.Structure):
         "committed_bytes", "executed_operations", "pending_events", "delivered_faults", "reclaimed_copy_bytes")]
 
 
+class TokenizerFactsC(ctypes.Structure):
+    _fields_ = [("model", ctypes.c_char_p), ("pre", ctypes.c_char_p), ("tokens", ctypes.c_void_p),
+                ("token_lens", ctypes.c_void_p), ("n_tokens", ctypes.c_uint64), ("token_types", ctypes.c_void_p),
+                ("n_token_types", ctypes.c_uint64), ("merges", ctypes.c_void_p), ("merge_lens", ctypes.c_void_p),
+                ("n_merges", ctypes.c_uint64), ("scores_present", ctypes.c_int32),
+                ("bos_token_id", ctypes.c_uint32), ("eos_token_id", ctypes.c_uint32),
+                ("pad_token_id", ctypes.c_uint32), ("unk_token_id", ctypes.c_uint32),
+                ("add_bos_token", ctypes.c_int32), ("add_space_prefix", ctypes.c_int32),
+                ("expected_vocab", ctypes.c_uint64), ("expected_merges", ctypes.c_uint64)]
+
+
 class FaberError(RuntimeError):
     """A failed C-ABI call: ``code`` is the FaberRtStatusV1 code."""
 
     def __init__(self, code: int, message: str):
         super().__init__(f"{STATUS_NAMES.get(code, code)}: {message}")
         self.code = code
+        self.message = message
         self.message = message
 
 
@@ -143,6 +155,12 @@ SIGNATURES = {
     "faber_gpu_v2_txn_backend_free": (Status, [P]),
     "faber_gpu_v2_tp_step_plan": (Status, [ctypes.POINTER(ModelConfigC), U32, P, U32, ctypes.POINTER(U32),
                                            ctypes.POINTER(U64), P]),
+    "faber_gpu_v2_gguf_kv_payload": (Status, [P, U64, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_tokenizer_create": (Status, [ctypes.POINTER(TokenizerFactsC), PP]),
+    "faber_gpu_v2_tokenizer_encode": (Status, [P, P, U64, I32, P, U64, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_tokenizer_decode": (Status, [P, P, U64, P, U64, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_tokenizer_info": (Status, [P, ctypes.POINTER(U64), P, P, U64, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_tokenizer_free": (Status, [P]),
     "faber_gpu_v2_model_create": (Status, [ctypes.POINTER(ModelConfigC), PP]),
     "faber_gpu_v2_model_set_tensor": (Status, [P, ctypes.c_char_p, U32, P, U64, U64, U64]),
     "faber_gpu_v2_tp_shard": (Status, [ctypes.POINTER(ModelConfigC), ctypes.c_char_p, P]),

@@ -18,6 +18,7 @@
 #include "gguf.hpp"
 #include "ops.cuh"
 #include "repack.hpp"
+#include "tokenizer.hpp"
 #include "transaction.hpp"
 
 namespace faber {
@@ -893,6 +894,107 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_get_str
 
 __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_free(FaberGguf* g) {
   return guarded("faber_gpu_v2_gguf_free", [&] { delete g; });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_gguf_kv_payload(const FaberGguf* g,
+                                                                                    uint64_t index,
+                                                                                    uint64_t* offset) {
+  return guarded("faber_gpu_v2_gguf_kv_payload", [&] {
+    FABER_ARG(g && offset, "null pointer");
+    FABER_ARG(index < g->f.kv.size(), "KV index out of range");
+    FABER_ARG(g->f.kv[index].type == GGUF_ARRAY, g->f.kv[index].key + " is not an array");
+    *offset = g->f.kv[index].payload;
+  });
+}
+
+// --- tokenizer (src/tokenizer/mod.rs) ----------------------------------------
+struct FaberTokenizer {
+  faber::tok::Tokenizer t;
+};
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_tokenizer_create(
+    const FaberTokenizerFactsV1* f, FaberTokenizer** out) {
+  return guarded("faber_gpu_v2_tokenizer_create", [&] {
+    FABER_ARG(f && out && f->model && f->pre, "null pointer");
+    *out = nullptr;
+    FABER_ARG((f->tokens && f->token_lens) || !f->n_tokens, "null token arrays");
+    FABER_ARG(f->token_types || !f->n_token_types, "null token types");
+    FABER_ARG((f->merges && f->merge_lens) || !f->n_merges, "null merge arrays");
+    faber::tok::Facts facts;
+    facts.model = f->model;
+    facts.pre = f->pre;
+    facts.tokens.reserve(f->n_tokens);
+    for (uint64_t i = 0; i < f->n_tokens; ++i) {
+      FABER_ARG(f->tokens[i] || !f->token_lens[i], "null token text");
+      facts.tokens.emplace_back(f->tokens[i] ? f->tokens[i] : "", f->token_lens[i]);
+    }
+    facts.token_types.assign(f->token_types, f->token_types + f->n_token_types);
+    facts.merges.reserve(f->n_merges);
+    for (uint64_t i = 0; i < f->n_merges; ++i) {
+      FABER_ARG(f->merges[i] || !f->merge_lens[i], "null merge text");
+      facts.merges.emplace_back(f->merges[i] ? f->merges[i] : "", f->merge_lens[i]);
+    }
+    facts.scores_present = f->scores_present != 0;
+    facts.bos = f->bos_token_id;
+    facts.eos = f->eos_token_id;
+    facts.pad = f->pad_token_id;
+    facts.unk = f->unk_token_id;
+    facts.add_bos = f->add_bos_token != 0;
+    facts.add_space_prefix = f->add_space_prefix != 0;
+    facts.expected_vocab = f->expected_vocab;
+    facts.expected_merges = f->expected_merges;
+    *out = new FaberTokenizer{faber::tok::Tokenizer(facts)};
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_tokenizer_encode(
+    const FaberTokenizer* t, const uint8_t* text, uint64_t len, int32_t parse_special, uint32_t* ids,
+    uint64_t cap, uint64_t* n_ids) {
+  return guarded("faber_gpu_v2_tokenizer_encode", [&] {
+    FABER_ARG(t && n_ids && (text || !len), "null pointer");
+    FABER_ARG(len <= faber::tok::kMaxInputBytes,
+              "InputTooLarge: encode input " + std::to_string(len) + " bytes exceeds 1 MiB");
+    const std::vector<uint32_t> v =
+        t->t.encode(std::string(reinterpret_cast<const char*>(text), (size_t)len), parse_special != 0);
+    *n_ids = v.size();
+    require(ids != nullptr && cap >= v.size(), FABER_STATUS_IO_ERROR,
+            "encoding needs " + std::to_string(v.size()) + " ids");
+    std::copy(v.begin(), v.end(), ids);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_tokenizer_decode(
+    const FaberTokenizer* t, const uint32_t* ids, uint64_t n, uint8_t* out, uint64_t cap, uint64_t* n_out) {
+  return guarded("faber_gpu_v2_tokenizer_decode", [&] {
+    FABER_ARG(t && n_out && (ids || !n), "null pointer");
+    const std::string s = t->t.decode(std::vector<uint32_t>(ids, ids + n));
+    *n_out = s.size();
+    require(out != nullptr && cap >= s.size(), FABER_STATUS_IO_ERROR,
+            "decoding needs " + std::to_string(s.size()) + " bytes");
+    std::memcpy(out, s.data(), s.size());
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_tokenizer_info(
+    const FaberTokenizer* t, uint64_t* vocab, uint32_t special_ids[4], uint32_t* eog, uint64_t eog_cap,
+    uint64_t* n_eog) {
+  return guarded("faber_gpu_v2_tokenizer_info", [&] {
+    FABER_ARG(t && vocab && special_ids && n_eog, "null pointer");
+    *vocab = t->t.vocab_size();
+    special_ids[0] = t->t.bos();
+    special_ids[1] = t->t.eos();
+    special_ids[2] = t->t.pad();
+    special_ids[3] = t->t.unk();
+    const auto& e = t->t.eog();
+    *n_eog = e.size();
+    require(eog != nullptr && eog_cap >= e.size(), FABER_STATUS_IO_ERROR,
+            "end-of-generation set has " + std::to_string(e.size()) + " ids");
+    std::copy(e.begin(), e.end(), eog);
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_tokenizer_free(FaberTokenizer* t) {
+  return guarded("faber_gpu_v2_tokenizer_free", [&] { delete t; });
 }
 
 // --- execution transaction (src/execution_transaction/transaction.rs) ------

@@ -183,8 +183,8 @@ class Transaction:
             _lib.call("faber_gpu_v2_txn_create", parts, len(partitions), ops, len(operations), barr, len(bb),
                       larr, len(bl), ctypes.byref(h))
         except _lib.FaberError as e:
-            kind = next((k for k in ERROR_KINDS[1:3] if k in str(e)), "")
-            raise TransactionError(e.code, str(e), kind) from None
+            kind = next((k for k in ERROR_KINDS[1:3] if k in e.message), "")
+            raise TransactionError(e.code, e.message, kind) from None
         self._h = h
 
     def _run(self, name: str, *args) -> None:
@@ -193,7 +193,7 @@ class Transaction:
         except _lib.FaberError as e:
             c = _lib.TxnErrorC()
             _lib.call("faber_gpu_v2_txn_last_error", self._h, ctypes.byref(c))
-            raise TransactionError(e.code, str(e), ERROR_KINDS[c.kind], c.partition,
+            raise TransactionError(e.code, e.message, ERROR_KINDS[c.kind], c.partition,
                                    BACKEND_CLASSES.get(c.backend_class, ""), c.budget_class, c.missing) from None
 
     def prepare(self, backend: FaultBackend) -> None:

@@ -486,6 +486,63 @@ FaberRtStatusV1 faber_gpu_v2_gguf_get_float(const FaberGguf* g, const char* key,
 FaberRtStatusV1 faber_gpu_v2_gguf_get_string(const FaberGguf* g, const char* key, char* buf,
                                              uint64_t cap, uint64_t* len);
 FaberRtStatusV1 faber_gpu_v2_gguf_free(FaberGguf* g);
+/* The buffer offset of an array KV's first element (strings: a u64 length,
+ * then the bytes, back to back), for reading arrays such as the tokenizer's
+ * from the parsed bytes. INVALID_ARGUMENT for a non-array KV. */
+FaberRtStatusV1 faber_gpu_v2_gguf_kv_payload(const FaberGguf* g, uint64_t index, uint64_t* offset);
+
+/* --- tokenizer (src/tokenizer/mod.rs) ---------------------------------------
+ * GPT-2 byte-level BPE with the `smollm` pre-tokenizer: text in, token ids
+ * out, for prompts given as text. Host-only. The facts are the GGUF's
+ * tokenizer.ggml.* metadata (Gpt2BpeTokenizer::new, mod.rs:329-530).
+ * Construction refuses, as INVALID_ARGUMENT whose message begins with the
+ * reference's TokenizerError kind: a model other than "gpt2"
+ * (UnsupportedModel), a pre-tokenizer other than "smollm"
+ * (UnsupportedPreTokenizer), vocabulary or merge counts other than the
+ * expected (VocabSizeMismatch, MergesCountMismatch), a token_type count
+ * other than the vocabulary's (TokenTypeCountMismatch), scores
+ * (ScoresPresent), add_bos_token or add_space_prefix set, a malformed merge
+ * (MalformedMergeString), an empty, overlong or space-holding token text
+ * (ByteBoundaryViolation), a special id out of range (TokenIdOutOfRange). */
+typedef struct FaberTokenizer FaberTokenizer;
+
+typedef struct FaberTokenizerFactsV1 {
+  const char* model;               /* tokenizer.ggml.model */
+  const char* pre;                 /* tokenizer.ggml.pre */
+  const char* const* tokens;       /* tokenizer.ggml.tokens (token_lens bytes each) */
+  const uint64_t* token_lens;
+  uint64_t n_tokens;
+  const int32_t* token_types;      /* tokenizer.ggml.token_type */
+  uint64_t n_token_types;
+  const char* const* merges;       /* tokenizer.ggml.merges (merge_lens bytes each) */
+  const uint64_t* merge_lens;
+  uint64_t n_merges;
+  int32_t scores_present;          /* tokenizer.ggml.scores exists */
+  uint32_t bos_token_id, eos_token_id, pad_token_id, unk_token_id;
+  int32_t add_bos_token, add_space_prefix;
+  uint64_t expected_vocab;         /* the pinned row: 49152 */
+  uint64_t expected_merges;        /* the pinned row: 48900 */
+} FaberTokenizerFactsV1;
+
+FaberRtStatusV1 faber_gpu_v2_tokenizer_create(const FaberTokenizerFactsV1* facts, FaberTokenizer** out);
+/* encode (mod.rs:690-770): UTF-8 text -> ids. parse_special turns control,
+ * unknown and user-defined token texts into their ids (user-defined ones
+ * always). *n_ids is always set; with cap below it the call is IO_ERROR and
+ * writes no ids (2 x len + 1024 is always enough). INVALID_ARGUMENT for
+ * invalid UTF-8 (InvalidUtf8) or more than 1 MiB (InputTooLarge). */
+FaberRtStatusV1 faber_gpu_v2_tokenizer_encode(const FaberTokenizer* t, const uint8_t* text, uint64_t len,
+                                              int32_t parse_special, uint32_t* ids, uint64_t cap,
+                                              uint64_t* n_ids);
+/* ids -> bytes: each token's text through the inverse byte map (special
+ * texts as they are). *n_out is always set; IO_ERROR when cap is short. */
+FaberRtStatusV1 faber_gpu_v2_tokenizer_decode(const FaberTokenizer* t, const uint32_t* ids, uint64_t n,
+                                              uint8_t* out, uint64_t cap, uint64_t* n_out);
+/* Vocabulary size, {bos, eos, pad, unk} ids and the end-of-generation ids
+ * (tokens with an end-of-turn text, then eos; *n_eog always set, IO_ERROR
+ * when eog_cap is short). */
+FaberRtStatusV1 faber_gpu_v2_tokenizer_info(const FaberTokenizer* t, uint64_t* vocab, uint32_t special_ids[4],
+                                            uint32_t* eog, uint64_t eog_cap, uint64_t* n_eog);
+FaberRtStatusV1 faber_gpu_v2_tokenizer_free(FaberTokenizer* t);
 
 /* Batched greedy decode — run_greedy (src/greedy_run.rs:186-248) for up to
  * 16 sequences in lockstep, the batch-16 decode of the reference's
