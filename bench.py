@@ -16,8 +16,8 @@ value      tokens/s over the K timed tokens (CUDA events on the decode
            stream, max over ranks), weights and KV resident in HBM
            (3.7 GB of weights per token: far larger than L2).
 e2e        tokens/s through the public API with host buffers: per token
-           position_logits (device->host copy of the logits), host argmax
-           over non-EOG ids, push_token (host->device copy of the id).
+           one step_greedy call (the id host->device from pinned memory,
+           the step and its greedy argmax, the next id device->host).
 roofline   the Q4_K dequant-GEMV (the dominant kernel) over this rank's
            7B layer shapes + head, replayed in a CUDA graph over three
            weight copies per shape (411 MB > L2), CUDA events.
@@ -325,7 +325,7 @@ def run_faber(args):
     ws, rank, local = dist_env()
     n = args.gpus
     torch.cuda.set_device(local)
-    from faber_runtime_b200 import LLAMA2_7B, ForwardRun, _lib, synth, top1_non_eog
+    from faber_runtime_b200 import LLAMA2_7B, ForwardRun, _lib, synth
     cfg = LLAMA2_7B
     uid = b""
     pg = None
@@ -373,9 +373,9 @@ def run_faber(args):
     value = args.steps / (ms * 1e-3)
     # end to end through the public API with host buffers
     t0 = time.perf_counter()
+    tok = int(toks[-1])
     for _ in range(args.e2e_steps):
-        lg = run.position_logits()
-        run.push_token(top1_non_eog(lg))
+        tok = run.step_greedy(tok)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     if pg:
@@ -396,7 +396,7 @@ def run_faber(args):
                                    f"{PREFILL} random ids, {args.steps} timed tokens",
                        "global_batch": 1, "seq_len": PREFILL, "parallelism": f"tp{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (3.7 GB weights per token)", "kv_dtype": "f16 (value-identical)"},
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * cfg.vocab},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
             "gpu_launches": launches_per_token * args.steps,
             "roofline": {"bound": "hbm", "achieved": roof["achieved_gbs"], "peak": peak, "unit": "GB/s",
                          "frac": roof["achieved_gbs"] / peak, "peak_kind": peak_kind,

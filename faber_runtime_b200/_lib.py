@@ -173,6 +173,7 @@ SIGNATURES = {
     "faber_gpu_v2_session_len": (Status, [P, ctypes.POINTER(U64)]),
     "faber_gpu_v2_session_push_token": (Status, [P, I64]),
     "faber_gpu_v2_session_push_tokens": (Status, [P, P, U64]),
+    "faber_gpu_v2_session_step_greedy": (Status, [P, I64, P, U32, ctypes.POINTER(I64)]),
     "faber_gpu_v2_session_position_logits": (Status, [P, P, U64]),
     "faber_gpu_v2_session_greedy": (Status, [P, U32, P, U32, P, ctypes.POINTER(I32)]),
     "faber_gpu_v2_session_set_prefix": (Status, [P, U32, P, P, U64]),

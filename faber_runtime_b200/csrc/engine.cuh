@@ -1313,6 +1313,39 @@ inline void run_greedy(SessionState& S, uint32_t n_gen, const int64_t* eog, uint
   (void)M;
 }
 
+// One step of a host-driven greedy loop: push `token`, then the new
+// position's logits and their argmax over the non-EOG ids, returning only
+// that id. The token travels in 8 bytes from pinned memory and the answer in
+// 8 bytes back; the logits stay on the device. The same graph as a
+// run_greedy step, so the ids equal run_greedy's.
+inline int64_t run_step_greedy(SessionState& S, int64_t token, const int64_t* eog, uint32_t n_eog) {
+  ModelState& M = S.m->s;
+  FABER_CUDA(cudaSetDevice(S.device));
+  FABER_ARG(n_eog <= (uint32_t)kMaxEog, "at most 8 EOG ids");
+  FABER_ARG(eog != nullptr || n_eog == 0, "null EOG ids");
+  FABER_ARG(token >= 0 && token < (int64_t)M.cfg.vocab,
+            "token " + std::to_string(token) + " is outside the vocab [0, " + std::to_string(M.cfg.vocab) + ")");
+  require(S.n + 1 <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
+  check_prefix_complete(S);
+  std::vector<int64_t> e(eog, eog + n_eog);
+  StepState* st = st_ptr(S);
+  int64_t* pin = static_cast<int64_t*>(S.pinned);
+  pin[0] = token;
+  FABER_CUDA(cudaMemcpyAsync(&st->input_token, pin, 8, cudaMemcpyHostToDevice, S.stream));
+  if (S.trace) {
+    enqueue_push(S, false);
+    enqueue_logits(S, false, e);
+  } else {
+    ensure_graphs(S, e);
+    FABER_CUDA(cudaGraphLaunch(S.g_step, S.stream));
+  }
+  FABER_CUDA(cudaMemcpyAsync(pin + 1, &st->input_token, 8, cudaMemcpyDeviceToHost, S.stream));
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  check_device_waits();
+  S.n += 1;
+  return pin[1];
+}
+
 // ---------------------------------------------------------------------------
 // Batched greedy decode: up to kBatchMax sessions of one model advance one
 // token per step together. Every linear layer is one tcgen05 Q4_K GEMM whose
@@ -1954,6 +1987,16 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_push_token(FaberGpuSession* s,
   return guarded("faber_gpu_v2_session_push_token", [&] {
     FABER_ARG(s, "null session");
     run_push(s->s, &token, 1);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_step_greedy(FaberGpuSession* s, int64_t token,
+                                                             const int64_t* eog, uint32_t n_eog,
+                                                             int64_t* next_token) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_step_greedy", [&] {
+    FABER_ARG(s && next_token, "null pointer");
+    *next_token = run_step_greedy(s->s, token, eog, n_eog);
   });
 }
 

@@ -130,6 +130,17 @@ class ForwardRun:
         self._check_tokens(np.array([token], np.int64))
         _lib.call("faber_gpu_v2_session_push_token", self._h, int(token))
 
+    def step_greedy(self, token: int, eog=()) -> int:
+        """Push ``token`` and return the greedy id of the new position (the
+        argmax over ids not in ``eog``): one step of a host-driven greedy
+        loop, with 8 bytes each way between host and device."""
+        self._check_tokens(np.array([token], np.int64))
+        e = np.ascontiguousarray(list(eog), dtype=np.int64)
+        nxt = _lib.I64()
+        _lib.call("faber_gpu_v2_session_step_greedy", self._h, int(token), e.ctypes.data if e.size else None,
+                  e.size, ctypes.byref(nxt))
+        return nxt.value
+
     def push_tokens(self, tokens) -> None:
         t = np.ascontiguousarray(tokens, dtype=np.int64)
         if t.size == 0:

@@ -444,6 +444,14 @@ FaberRtStatusV1 faber_gpu_v2_session_push_token(FaberGpuSession* s, int64_t toke
 /* Append n tokens (the prompt) — same as n push_token calls. */
 FaberRtStatusV1 faber_gpu_v2_session_push_tokens(FaberGpuSession* s, const int64_t* tokens,
                                                  uint64_t n);
+/* One step of a host-driven greedy loop (run_greedy's step,
+ * src/greedy_run.rs:186-248, with the host choosing each input): push
+ * `token`, then write the argmax of the new position's logits over the ids
+ * not in eog[0..n_eog) (top1_non_eog, src/cpu_oracle.rs:980-1016) to
+ * *next_token. Only those 8 bytes leave the device; the ids equal
+ * session_greedy's. Errors as push_token. */
+FaberRtStatusV1 faber_gpu_v2_session_step_greedy(FaberGpuSession* s, int64_t token, const int64_t* eog,
+                                                 uint32_t n_eog, int64_t* next_token);
 /* ForwardRun::position_logits (src/cpu_oracle.rs:920-926): full-vocab raw
  * logits at the sequence end into a host buffer of cap floats. */
 FaberRtStatusV1 faber_gpu_v2_session_position_logits(FaberGpuSession* s, float* logits,

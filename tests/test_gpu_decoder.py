@@ -66,6 +66,26 @@ def test_tiny_greedy_token_identical_and_logits_close(tiny):
     assert len(run) == 32 + 64
 
 
+def test_step_greedy_follows_session_greedy(tiny):
+    """A host-driven loop of step_greedy (push the id, read back the next)
+    yields the same ids as session greedy, with and without EOG ids."""
+    from faber_runtime_b200 import ForwardRun, synth
+    _, dm, _ = tiny
+    prompt = synth.tokens(2024, 9, 20, 32000)
+    for eog in ((), (5, 17)):
+        ref = ForwardRun(dm, prompt, context_length=64)
+        want, _ = ref.greedy(12, eog=eog)
+        ref.close()
+        run = ForwardRun(dm, prompt, context_length=64)
+        first, _ = run.greedy(1, eog=eog)
+        got = [int(first[0])]
+        for _ in range(11):
+            got.append(run.step_greedy(got[-1], eog=eog))
+        assert got == want.tolist()
+        assert len(run) == 20 + 11
+        run.close()
+
+
 def test_tiny_forward_one_matches(tiny):
     import oracle as o
     from faber_runtime_b200 import synth
