@@ -270,3 +270,28 @@ def admitted(transfer_staging_bytes: int, activation_scratch_bytes: int, **class
     """A ledger with the two classes a transaction reserves against."""
     return PartitionLedger(transfer_staging_bytes=transfer_staging_bytes,
                            activation_scratch_bytes=activation_scratch_bytes, **classes)
+
+
+def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=None) -> Receipt:
+    """Execute this rank's transaction, then agree with every rank of the
+    process group on the outcome before anything is published: commit only
+    when every rank executed its step, abort everywhere otherwise. A rank
+    that fails, or a collective that fails (a rank that died or never
+    joined, ending in the group's timeout), makes every rank abort."""
+    import torch
+    import torch.distributed as dist
+    reason = ""
+    try:
+        t.execute(backend)
+        ok = 1
+    except TransactionError as e:
+        ok, reason = 0, f"{e.kind} on partition {e.partition}"
+    flag = torch.tensor([ok], dtype=torch.int32)
+    try:
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    except Exception as e:  # the group itself failed
+        flag[0] = 0
+        reason = reason or f"group decision failed: {type(e).__name__}"
+    if int(flag.item()) == 1:
+        return t.commit(backend, ordinal)
+    return t.abort(backend, reason or "another rank failed")

@@ -1,0 +1,82 @@
+"""The group decision of a tensor-parallel step on 2 gloo ranks (CPU): each
+rank runs the step's transaction, and the ranks agree before anything is
+published. Failures are made on the host: a fault injected into one
+rank's backend, and a rank that dies before the decision. No GPU is used.
+"""
+
+import multiprocessing as mp
+import os
+import socket
+from datetime import timedelta
+
+WORLD = 2
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, port, mode, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from faber_runtime_b200 import LLAMA2_7B, partition
+    from faber_runtime_b200 import transaction as tx
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=20))
+    try:
+        cfg = LLAMA2_7B.with_layers(2)
+        ops, barriers, launches = tx.tp_step_plan(cfg, WORLD, 300)
+        ledgers = {r: partition.plan(cfg, 512, tp_size=WORLD, tp_rank=r) for r in range(WORLD)}
+        t, b = tx.Transaction(ledgers, ops, barriers, launches), tx.FaultBackend()
+        t.prepare(b)
+        if mode == "fault" and rank == 1:
+            b.inject(ops[1], 1, tx.KERNEL_ERROR)  # this rank's own step fails
+        if mode == "dies" and rank == 1:
+            os._exit(3)  # gone before the decision, nothing in flight
+        r = tx.run_group_step(t, b, ordinal=300)
+        q.put((rank, r.decision, r.published_bytes, b.info()["committed_bytes"], r.failure_kind))
+    except Exception as e:  # reported, not hidden
+        q.put((rank, "error", repr(e), 0, ""))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_rank, args=(r, port, mode, q)) for r in range(WORLD)]
+    for p in ps:
+        p.start()
+    expect = 1 if mode == "dies" else WORLD
+    out = sorted(q.get(timeout=120) for _ in range(expect))
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_every_rank_commits_when_every_step_ran():
+    out = _run("ok")
+    assert [o[1] for o in out] == ["Committed"] * WORLD
+    assert out[0][2] == out[1][2] > 0 and all(o[3] == o[2] for o in out)
+
+
+def test_one_rank_failing_aborts_every_rank():
+    out = _run("fault")
+    assert [o[1] for o in out] == ["Aborted"] * WORLD, out
+    assert all(o[2] == 0 and o[3] == 0 for o in out)  # nothing published anywhere
+    assert out[1][4] == "Backend" and out[0][4] == "Cancelled"
+
+
+def test_a_rank_that_dies_aborts_the_survivor():
+    out = _run("dies")
+    assert len(out) == 1 and out[0][0] == 0
+    assert out[0][1] == "Aborted" and out[0][2] == 0, out
