@@ -12,6 +12,7 @@ device work, and a failed C-ABI call raises ``FaberError`` with its status.
 from __future__ import annotations
 
 import ctypes
+import json
 from dataclasses import dataclass, field
 from typing import Iterable
 
@@ -241,6 +242,7 @@ class GreedyDivergence:
     comparator_trace_token: int
     oracle_token: int
     failing_thresholds: list = field(default_factory=lambda: ["top-1"])
+    max_band_deviation: float | None = None
 
 
 @dataclass
@@ -257,6 +259,60 @@ class GreedyRunRecord:
             return "none"
         return (f"position {d.position} (comparator {d.comparator_trace_token} vs oracle "
                 f"{d.oracle_token}; {','.join(d.failing_thresholds)})")
+
+
+RECORD_SCHEMA = "gi2-4-greedy-record-v1"
+
+
+def _tokens_sha256(tokens) -> str:
+    """SHA-256 of the ids as little-endian u64s (src/greedy_run.rs:342-350)."""
+    import hashlib
+    return hashlib.sha256(np.asarray(tokens, dtype=np.int64).astype("<u8").tobytes()).hexdigest()
+
+
+def record_to_json(record: GreedyRunRecord, prompt_tokens, trace: dict | None = None) -> str:
+    """The committed-record wire format (record_to_json,
+    src/greedy_run.rs:271-340): one compact JSON object with sorted keys and
+    a trailing newline. ``trace`` is the comparator trace's provenance
+    object, when the run followed one."""
+    d = record.first_divergence
+    root = {
+        "schema": RECORD_SCHEMA,
+        "prompt_tokens": [int(t) for t in prompt_tokens],
+        "generated_token_count": len(record.generated_tokens),
+        "all_finite": bool(record.all_finite),
+        "all_agree": d is None,
+        "generated_tokens": [int(t) for t in record.generated_tokens],
+        "generated_tokens_sha256": _tokens_sha256(record.generated_tokens),
+        "first_divergence": None if d is None else {
+            "position": d.position, "comparator_trace_token": d.comparator_trace_token,
+            "oracle_token": d.oracle_token, "failing_thresholds": list(d.failing_thresholds),
+            "max_band_deviation": d.max_band_deviation},
+    }
+    if trace is not None:
+        root["trace"] = trace
+    return json.dumps(root, sort_keys=True, separators=(",", ":")) + "\n"
+
+
+def record_from_json(text: str):
+    """(GreedyRunRecord, prompt tokens, trace provenance or None) from the
+    committed-record wire format; refuses another schema, a count or hash
+    that contradicts the tokens, and all_agree contradicting the divergence."""
+    root = json.loads(text)
+    if root.get("schema") != RECORD_SCHEMA:
+        raise OracleError("RecordSchema", f"schema {root.get('schema')!r} is not {RECORD_SCHEMA!r}")
+    toks = [int(t) for t in root["generated_tokens"]]
+    if root["generated_token_count"] != len(toks):
+        raise OracleError("RecordCount", "generated_token_count does not match the tokens")
+    if root["generated_tokens_sha256"] != _tokens_sha256(toks):
+        raise OracleError("RecordHash", "generated_tokens_sha256 does not match the tokens")
+    dv = root["first_divergence"]
+    if root["all_agree"] != (dv is None):
+        raise OracleError("RecordAgreement", "all_agree contradicts first_divergence")
+    div = None if dv is None else GreedyDivergence(
+        int(dv["position"]), int(dv["comparator_trace_token"]), int(dv["oracle_token"]),
+        list(dv["failing_thresholds"]), dv.get("max_band_deviation"))
+    return GreedyRunRecord(toks, bool(root["all_finite"]), div), root["prompt_tokens"], root.get("trace")
 
 
 def run_greedy(model: DeviceModel, prompt, trace_tokens, eog=(), context_length: int | None = None,

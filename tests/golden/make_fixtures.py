@@ -9,9 +9,13 @@ reference manifest records, and writes:
   op_goldens.npz   - float32 arrays "<op>.<input name>" and "<op>.expected"
   op_goldens.json  - per-op scalar parameters, input names, expected SHA-256
   logits_pos0.npz  - "raw_logits" (49152 f32), "logp", top-1 ids
+  greedy_record.json           - the committed 256-token greedy run record
+                                 (testdata/gi2-4-greedy-record/record.json, bytes unchanged)
+  greedy_record_manifest.json  - its manifest (SHA-256, token count)
 
 Run from the repository root in an environment that has the reference tree:
     python tests/golden/make_fixtures.py /root/reference
+    python tests/golden/make_fixtures.py /root/reference record   # the record files only
 The GPU-side tests read only the outputs, never the reference tree.
 """
 
@@ -81,5 +85,20 @@ def main(ref_root: str) -> None:
     print("wrote", HERE / "op_goldens.npz", HERE / "logits_pos0.npz")
 
 
+def record(ref_root: str) -> None:
+    rdir = Path(ref_root) / "testdata" / "gi2-4-greedy-record"
+    man = json.loads((rdir / "manifest.json").read_text())
+    raw = (rdir / "record.json").read_bytes()
+    assert hashlib.sha256(raw).hexdigest() == man["fixtures"][0]["sha256"], "record.json sha256 mismatch"
+    (HERE / "greedy_record.json").write_bytes(raw)
+    (HERE / "greedy_record_manifest.json").write_text(json.dumps(man, indent=1, sort_keys=True) + "\n")
+    print("wrote", HERE / "greedy_record.json")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) > 2 and sys.argv[2] == "record":
+        record(root)
+    else:
+        main(root)
+        record(root)
