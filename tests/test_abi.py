@@ -129,3 +129,41 @@ def test_model_config_byte_accounting(faber):
     assert LLAMA2_7B.head_bytes() == 73_728_000
     assert LLAMA3_70B.linear_bytes() == 38_503_710_720
     assert LLAMA3_70B.head_bytes() == 591_003_648
+
+
+def test_upload_fail_closed_matrix_on_the_host(faber):
+    """The dequant fail-closed matrix (src/dequant_test.rs:423-574,775-839)
+    at the C ABI: exact byte lengths, whole blocks, known types and non-null
+    buffers are checked on the host before any device work, so every
+    refusal here is INVALID_ARGUMENT with no GPU present."""
+    import ctypes
+
+    import numpy as np
+    from faber_runtime_b200 import _lib
+    L = _lib.lib()
+    out = ctypes.c_void_p()
+    ok = np.zeros(144, np.uint8)
+    for nbytes, rows, cols in [(143, 1, 256), (145, 1, 256), (0, 1, 256), (288, 1, 256),  # byte lengths
+                               (144, 0, 256), (144, 1, 0), (144, 1, 128),                  # shapes
+                               (144 * 3, 3, 255)]:                                        # not whole blocks
+        buf = np.zeros(max(nbytes, 1), np.uint8)
+        st = L.faber_gpu_v2_q4k_upload(buf.ctypes.data, nbytes, rows, cols, ctypes.byref(out))
+        assert st.code == _lib.INVALID_ARGUMENT, (nbytes, rows, cols)
+    assert L.faber_gpu_v2_q4k_upload(None, 144, 1, 256, ctypes.byref(out)).code == _lib.INVALID_ARGUMENT
+    assert L.faber_gpu_v2_q4k_upload(ok.ctypes.data, 144, 1, 256, None).code == _lib.INVALID_ARGUMENT
+    # typed rows: per type the exact bytes of whole blocks (Q8_0 34 B / 32, Q5_0 22 B / 32, Q6_K 210 B / 256)
+    for gtype, be, bb in [(8, 32, 34), (6, 32, 22), (14, 256, 210)]:
+        good = 2 * (64 // be if be == 32 else 1) * bb
+        cols = 64 if be == 32 else 256
+        for nbytes in (good - 1, good + 1, 0):
+            buf = np.zeros(max(nbytes, 1), np.uint8)
+            st = L.faber_gpu_v2_typed_upload(gtype, buf.ctypes.data, nbytes, 2, cols, ctypes.byref(out))
+            assert st.code == _lib.INVALID_ARGUMENT, (gtype, nbytes)
+        st = L.faber_gpu_v2_typed_upload(gtype, ok.ctypes.data, good, 2, cols + 1, ctypes.byref(out))
+        assert st.code == _lib.INVALID_ARGUMENT  # ragged rows
+    for bad_type in (2, 3, 10, 13, 99):  # Q4_0, Q4_1, Q2_K, Q5_K, unknown: not admitted
+        assert L.faber_gpu_v2_typed_upload(bad_type, ok.ctypes.data, 144, 1, 256,
+                                           ctypes.byref(out)).code == _lib.INVALID_ARGUMENT
+        assert L.faber_gpu_v2_dequant_blocks(bad_type, ok.ctypes.data, 1, None, 1,
+                                             None).code == _lib.INVALID_ARGUMENT
+    assert L.faber_gpu_v2_dequant_blocks(12, None, 1, None, 1, None).code == _lib.INVALID_ARGUMENT
