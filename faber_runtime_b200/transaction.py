@@ -272,20 +272,32 @@ def admitted(transfer_staging_bytes: int, activation_scratch_bytes: int, **class
                            activation_scratch_bytes=activation_scratch_bytes, **classes)
 
 
-def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=None) -> Receipt:
+def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=None, step=None,
+                   publish=None) -> Receipt:
     """Execute this rank's transaction, then agree with every rank of the
     process group on the outcome before anything is published: commit only
-    when every rank executed its step, abort everywhere otherwise. A rank
-    that fails, or a collective that fails (a rank that died or never
-    joined, ending in the group's timeout), makes every rank abort."""
+    when every rank executed its step, abort everywhere otherwise.
+
+    ``step`` is this rank's device work for the position (for example
+    ``lambda: run.step_greedy(token)``); a FaberError from it (a TIMEOUT of
+    a bounded exchange wait, DEVICE_LOSS, ...) counts as this rank failing.
+    ``publish(result)`` runs only after the group committed (for example
+    the session's token commit). A rank that fails, or a collective that
+    fails (a rank that died or never joined, ending in the group's
+    timeout), makes every rank abort; the aborted position is then not
+    committed on any rank."""
     import torch
     import torch.distributed as dist
-    reason = ""
+    reason, result = "", None
     try:
         t.execute(backend)
+        if step is not None:
+            result = step()
         ok = 1
     except TransactionError as e:
         ok, reason = 0, f"{e.kind} on partition {e.partition}"
+    except _lib.FaberError as e:
+        ok, reason = 0, f"step failed: {_lib.STATUS_NAMES.get(e.code, e.code)}"
     flag = torch.tensor([ok], dtype=torch.int32)
     try:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
@@ -293,5 +305,8 @@ def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=No
         flag[0] = 0
         reason = reason or f"group decision failed: {type(e).__name__}"
     if int(flag.item()) == 1:
-        return t.commit(backend, ordinal)
+        receipt = t.commit(backend, ordinal)
+        if publish is not None:
+            publish(result)
+        return receipt
     return t.abort(backend, reason or "another rank failed")

@@ -36,10 +36,18 @@ def _rank(rank, port, mode, q):
             b.inject(ops[1], 1, tx.KERNEL_ERROR)  # this rank's own step fails
         if mode == "dies" and rank == 1:
             os._exit(3)  # gone before the decision, nothing in flight
-        r = tx.run_group_step(t, b, ordinal=300)
-        q.put((rank, r.decision, r.published_bytes, b.info()["committed_bytes"], r.failure_kind))
+        published = []
+
+        def step():  # this rank's device work; rank 1's exchange wait expires in "timeout"
+            if mode == "timeout" and rank == 1:
+                from faber_runtime_b200 import _lib
+                raise _lib.FaberError(_lib.TIMEOUT, "a tensor-parallel peer did not publish its partials in time")
+            return 1000 + rank
+
+        r = tx.run_group_step(t, b, ordinal=300, step=step, publish=published.append)
+        q.put((rank, r.decision, r.published_bytes, b.info()["committed_bytes"], r.failure_kind, published))
     except Exception as e:  # reported, not hidden
-        q.put((rank, "error", repr(e), 0, ""))
+        q.put((rank, "error", repr(e), 0, "", []))
     finally:
         try:
             dist.destroy_process_group()
@@ -74,6 +82,18 @@ def test_one_rank_failing_aborts_every_rank():
     assert [o[1] for o in out] == ["Aborted"] * WORLD, out
     assert all(o[2] == 0 and o[3] == 0 for o in out)  # nothing published anywhere
     assert out[1][4] == "Backend" and out[0][4] == "Cancelled"
+
+
+def test_a_step_timeout_on_one_rank_aborts_every_rank():
+    out = _run("timeout")
+    assert [o[1] for o in out] == ["Aborted"] * WORLD, out
+    assert all(o[2] == 0 and o[5] == [] for o in out)  # nothing published, no token committed
+    assert out[1][4] == "Cancelled"  # the step failed outside the backend: aborted with its reason
+
+
+def test_publish_runs_only_after_the_group_commits():
+    out = _run("ok")
+    assert [o[5] for o in out] == [[1000], [1001]]
 
 
 def test_a_rank_that_dies_aborts_the_survivor():
