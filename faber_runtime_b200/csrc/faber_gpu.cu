@@ -725,7 +725,10 @@ inline void attention_decode_static(const float* q, const void* k_cache, const v
   static_check(n_heads <= (uint32_t)kStaticAttnMaxHeads &&
                    n_kv_heads <= (uint32_t)kStaticAttnMaxKvHeads,
                kBad, "the static attention scratch holds at most 128 query heads and 128 kv heads");
-  static_check(n_kv >= 1 && n_kv <= (uint64_t)INT32_MAX, kBad, "n_kv must be in [1, 2^31 - 1]");
+  // the kernel counts positions and 32-position groups in int: n_kv + 31
+  // must not overflow
+  static_check(n_kv >= 1 && n_kv <= (uint64_t)(INT32_MAX - kAttnGroup), kBad,
+               "n_kv must be in [1, 2^31 - 33]");
   int dev = 0, sms = 0;
   FABER_CUDA(cudaGetDevice(&dev));
   FABER_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

@@ -30,14 +30,6 @@
 
 #include "common.cuh"
 
-// Weight formation: 3 = f16 magics + exact sc*q + mixed-precision FMA (the
-// default, fewest ALU-pipe instructions); 1 = one mask-or per nibble against
-// the 2^23 f32 magic; 2 = byte permute; 0 = plain C expressions. All four
-// produce bit-identical weights.
-#ifndef FABER_DQ_MODE
-#define FABER_DQ_MODE 3
-#endif
-
 namespace faber {
 
 // PRO_NORM_RES: x = x + x2 (the residual add deferred from a tensor-parallel
@@ -470,49 +462,6 @@ __device__ __forceinline__ void q4_load(const GemvArgs& a, int tile, int b, int 
   }
 }
 
-// Per-row scale constants for this lane's two sub-blocks (2t low nibbles,
-// 2t+1 high nibbles): get_scale_min_k4 (src/dequant.rs:178-187) for all
-// eight sub-blocks at once as packed bytes, then d1 = d*sc, m1 = dmin*m.
-struct RowScales {
-  float2 lo01, lo23, hi01, hi23;  // d1 and d2 pre-scaled per nibble position
-  float2 nm1, nm2;                // (-m1, -m1), (-m2, -m2)
-};
-
-__device__ __forceinline__ RowScales row_scales(const uint4 h, int t) {
-  const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
-  const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-  const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
-  uint32_t sc, mm;
-  if (t < 2) {
-    sc = s0 & 0x3f3f3f3fu;
-    mm = s1 & 0x3f3f3f3fu;
-  } else {
-    sc = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
-    mm = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
-  }
-  const int sh = (t & 1) * 16;
-  const float sc_lo = (float)((sc >> sh) & 0xffu), sc_hi = (float)((sc >> (sh + 8)) & 0xffu);
-  const float m_lo = (float)((mm >> sh) & 0xffu), m_hi = (float)((mm >> (sh + 8)) & 0xffu);
-  const float d1 = __fmul_rn(d, sc_lo), d2 = __fmul_rn(d, sc_hi);
-  const float m1 = __fmul_rn(dmin, m_lo), m2 = __fmul_rn(dmin, m_hi);
-  RowScales r;
-#if FABER_DQ_MODE == 2
-  r.lo01 = r.lo23 = make_float2(d1, d1);
-  r.hi01 = r.hi23 = make_float2(d2, d2);
-#else
-  r.lo01 = make_float2(d1, d1 * 0x1p-8f);
-  r.lo23 = make_float2(d1 * 0x1p-16f, d1 * 0x1p-12f);
-  r.hi01 = make_float2(d2 * 0x1p-4f, d2 * 0x1p-12f);
-  r.hi23 = make_float2(d2 * 0x1p-8f, d2 * 0x1p-16f);
-#endif
-  r.nm1 = make_float2(-m1, -m1);
-  r.nm2 = make_float2(-m2, -m2);
-  return r;
-}
-
-// Dequantize the 8 nibbles of one quant word into four f16x2 A-operand
-// registers: lo = (e, e+1), (e+2, e+3) of the low sub-block; hi = the same
-// slots of the high sub-block.
 // One-instruction (w & MASK) | magic, with the magic in a register operand.
 template <uint32_t MASK>
 __device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t magic) {
@@ -528,47 +477,8 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b) {
   return d;
 }
 
-__device__ __forceinline__ void dequant_word(uint32_t w, const RowScales& s, uint32_t& lo0,
-                                             uint32_t& lo2, uint32_t& hi0, uint32_t& hi2,
-                                             uint32_t magic) {
-  const float2 negM = make_float2(-8388608.0f, -8388608.0f);
-  float2 f01, f23, h01, h23;
-#if FABER_DQ_MODE == 2
-  // byte permute: each nibble (pre-masked to a byte) lands in the magic's
-  // low mantissa byte, so every weight uses the unscaled d1 / d2
-  const uint32_t vl = w & 0x0f0f0f0fu, vh = (w >> 4) & 0x0f0f0f0fu;
-  f01 = make_float2(u2f(prmt<0x7540>(vl, magic)), u2f(prmt<0x7541>(vl, magic)));
-  f23 = make_float2(u2f(prmt<0x7542>(vl, magic)), u2f(prmt<0x7543>(vl, magic)));
-  h01 = make_float2(u2f(prmt<0x7540>(vh, magic)), u2f(prmt<0x7541>(vh, magic)));
-  h23 = make_float2(u2f(prmt<0x7542>(vh, magic)), u2f(prmt<0x7543>(vh, magic)));
-#elif FABER_DQ_MODE == 1
-  // the nibble stays at its bit position (<= bit 19) inside the 2^23 magic's
-  // mantissa; the per-position power of two is folded into the scale
-  const uint32_t u = w >> 12;
-  f01 = make_float2(u2f(and_or<0x0000000fu>(w, magic)), u2f(and_or<0x00000f00u>(w, magic)));
-  f23 = make_float2(u2f(and_or<0x000f0000u>(w, magic)), u2f(and_or<0x0000f000u>(u, magic)));
-  h01 = make_float2(u2f(and_or<0x000000f0u>(w, magic)), u2f(and_or<0x0000f000u>(w, magic)));
-  h23 = make_float2(u2f(and_or<0x00000f00u>(u, magic)), u2f(and_or<0x000f0000u>(u, magic)));
-#else
-  const uint32_t M = magic;
-  const uint32_t u = w >> 12;
-  f01 = make_float2(u2f((w & 0x0000000fu) | M), u2f((w & 0x00000f00u) | M));
-  f23 = make_float2(u2f((w & 0x000f0000u) | M), u2f((u & 0x0000f000u) | M));
-  h01 = make_float2(u2f((w & 0x000000f0u) | M), u2f((w & 0x0000f000u) | M));
-  h23 = make_float2(u2f((u & 0x00000f00u) | M), u2f((u & 0x000f0000u) | M));
-#endif
-  f01 = __ffma2_rn(__fadd2_rn(f01, negM), s.lo01, s.nm1);
-  f23 = __ffma2_rn(__fadd2_rn(f23, negM), s.lo23, s.nm1);
-  h01 = __ffma2_rn(__fadd2_rn(h01, negM), s.hi01, s.nm2);
-  h23 = __ffma2_rn(__fadd2_rn(h23, negM), s.hi23, s.nm2);
-  lo0 = pack_half2(f01.x, f01.y);
-  lo2 = pack_half2(f23.x, f23.y);
-  hi0 = pack_half2(h01.x, h01.y);
-  hi2 = pack_half2(h23.x, h23.y);
-}
-
 // ---------------------------------------------------------------------------
-// Mode 3: two nibbles per mask via f16 magics, exact sc*q in f16, and a
+// Weight formation: two nibbles per mask via f16 magics, exact sc*q in f16, and a
 // mixed-precision FMA for RN32(d*(sc*q) - m1).
 //   (w & 0x000F000F) | 0x64006400 = (1024 + q, 1024 + q') as f16x2;
 //   (w & 0x00F000F0) | 0x54005400 = (64 + q, 64 + q') (high nibbles);
@@ -690,14 +600,8 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 // are never read.
 __device__ __forceinline__ void q4_compute(const Q4Regs& r, int t, const __half* xsrc, int xbase,
                                            float (&acc)[4][4], const LaneConst& lc) {
-#if FABER_DQ_MODE == 3
   const RowScales3 sA = row_scales3(r.hA, t, lc);
   const RowScales3 sB = row_scales3(r.hB, t, lc);
-#else
-  const uint32_t magic = lc.m1024;
-  const RowScales sA = row_scales(r.hA, t);
-  const RowScales sB = row_scales(r.hB, t);
-#endif
 #pragma unroll
   for (int pp = 0; pp < 2; ++pp) {
     const uint4 qa = pp ? r.qA1 : r.qA0;
@@ -716,13 +620,8 @@ __device__ __forceinline__ void q4_compute(const Q4Regs& r, int t, const __half*
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t aL0, aL2, aH0, aH2, bL0, bL2, bH0, bH2;
-#if FABER_DQ_MODE == 3
       dequant_word3(word_of(qa, i), sA, lc, aL0, aL2, aH0, aH2);
       dequant_word3(word_of(qb, i), sB, lc, bL0, bL2, bH0, bH2);
-#else
-      dequant_word(word_of(qa, i), sA, aL0, aL2, aH0, aH2, magic);
-      dequant_word(word_of(qb, i), sB, bL0, bL2, bH0, bH2, magic);
-#endif
       const uint4& xl = (i < 2) ? xb_lo0 : xb_lo1;
       const uint4& xh = (i < 2) ? xb_hi0 : xb_hi1;
       const uint32_t xl0 = (i & 1) ? xl.z : xl.x, xl1 = (i & 1) ? xl.w : xl.y;
@@ -1118,7 +1017,7 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
 
   // consumers
   pdl_wait();
-  const float out_scale = stage_x<PRO, true, (FABER_DQ_MODE == 3)>(a, xh, xl, redd, redf);
+  const float out_scale = stage_x<PRO, true, true>(a, xh, xl, redd, redf);
   pdl_launch_dependents();
   const int g = lane >> 2, t = lane & 3;
   const __half* xsrc = (g == 0) ? xh : xl;
@@ -1126,11 +1025,7 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
   {
     const uint32_t k = 2u * (uint32_t)(t & 1);
     lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
-#if FABER_DQ_MODE == 3
     asm("mov.b32 %0, 0x64006400;" : "=r"(lc.m1024));
-#else
-    asm("mov.b32 %0, 0x4b000000;" : "=r"(lc.m1024));
-#endif
     asm("mov.b32 %0, 0x54005400;" : "=r"(lc.m64));
   }
   const uint8_t* my_item = ring + warp * kTileItemBytes;

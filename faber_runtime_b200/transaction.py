@@ -279,16 +279,26 @@ def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=No
     when every rank executed its step, abort everywhere otherwise.
 
     ``step`` is this rank's device work for the position (for example
-    ``lambda: run.step_greedy(token)``); a FaberError from it (a TIMEOUT of
-    a bounded exchange wait, DEVICE_LOSS, ...) counts as this rank failing.
+    ``lambda: run.step_greedy(token)``). Any exception from it counts as
+    this rank failing: a FaberError (a TIMEOUT of a bounded exchange wait,
+    DEVICE_LOSS, ...), and also any other error, such as the OracleError a
+    rejected token id raises. The rank still joins the group's vote, so the
+    other ranks abort at once instead of waiting for the group's timeout.
+    After the abort, an error that is not a FaberError or TransactionError
+    is raised again, so that a programming error is not mistaken for a
+    device fault.
+
     ``publish(result)`` runs only after the group committed (for example
     the session's token commit). A rank that fails, or a collective that
     fails (a rank that died or never joined, ending in the group's
-    timeout), makes every rank abort; the aborted position is then not
-    committed on any rank."""
+    timeout), makes every rank abort; nothing is published on any rank.
+    The device state is not rolled back: on a rank whose step ran, the
+    session has already written that position's K/V rows and advanced its
+    length, so after an abort the caller resets the session and replays its
+    committed tokens before the next step."""
     import torch
     import torch.distributed as dist
-    reason, result = "", None
+    reason, result, foreign = "", None, None
     try:
         t.execute(backend)
         if step is not None:
@@ -298,6 +308,8 @@ def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=No
         ok, reason = 0, f"{e.kind} on partition {e.partition}"
     except _lib.FaberError as e:
         ok, reason = 0, f"step failed: {_lib.STATUS_NAMES.get(e.code, e.code)}"
+    except Exception as e:  # noqa: BLE001 - the vote must happen whatever failed
+        ok, reason, foreign = 0, f"step raised {type(e).__name__}: {e}", e
     flag = torch.tensor([ok], dtype=torch.int32)
     try:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
@@ -309,4 +321,7 @@ def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=No
         if publish is not None:
             publish(result)
         return receipt
-    return t.abort(backend, reason or "another rank failed")
+    receipt = t.abort(backend, reason or "another rank failed")
+    if foreign is not None:
+        raise foreign
+    return receipt

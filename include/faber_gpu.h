@@ -637,7 +637,7 @@ FaberRtStatusV1 faber_gpu_v2_nccl_unique_id(uint8_t out[128]);
  * the counters first; the other contents are written before they are read.
  *
  * Limits: head_dim 64 or 128; n_heads and n_kv_heads at most 128; at most
- * 8 query heads per kv head; 1 <= n_kv < 2^31. Sizes beyond these return
+ * 8 query heads per kv head; 1 <= n_kv <= 2^31 - 33. Sizes beyond these return
  * INVALID_ARGUMENT with a message, before any work is queued.
  *
  * Set-up: the first call on a device looks up the array's device address

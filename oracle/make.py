@@ -12,16 +12,22 @@ from pathlib import Path
 
 _HERE = Path(__file__).resolve().parent
 SRC = _HERE / "faber_oracle.cpp"
+# The seeded input generator (plain C++, no GPU code) is linked in as well,
+# so that a CPU-only user of the oracle (the benchmark's reference leg)
+# draws the same synthetic weights without loading the GPU library.
+ROOT = _HERE.parent
+SYNTH = ROOT / "faber_runtime_b200" / "csrc" / "synth.cpp"
 OUT = _HERE / "_build" / "libfaber_oracle.so"
 
 
 def build(force: bool = False) -> Path:
-    if OUT.exists() and not force and OUT.stat().st_mtime >= SRC.stat().st_mtime:
+    srcs = [SRC, SYNTH]
+    if OUT.exists() and not force and all(OUT.stat().st_mtime >= s.stat().st_mtime for s in srcs):
         return OUT
     OUT.parent.mkdir(parents=True, exist_ok=True)
     cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off",
            "-fno-fast-math", "-fno-finite-math-only", "-fopenmp", "-fvisibility=hidden",
-           str(SRC), "-o", str(OUT)]
+           "-I", str(ROOT / "include"), *[str(s) for s in srcs], "-o", str(OUT), "-lpthread"]
     subprocess.run(cmd, check=True)
     return OUT
 

@@ -13,9 +13,10 @@ reference manifest records, and writes:
                                  (testdata/gi2-4-greedy-record/record.json, bytes unchanged)
   greedy_record_manifest.json  - its manifest (SHA-256, token count)
 
-Run from the repository root in an environment that has the reference tree:
-    python tests/golden/make_fixtures.py /root/reference
-    python tests/golden/make_fixtures.py /root/reference record   # the record files only
+Run from the repository root in an environment that has the reference tree,
+giving the path of the faber-runtime checkout as the first argument:
+    python tests/golden/make_fixtures.py <faber-runtime checkout>
+    python tests/golden/make_fixtures.py <faber-runtime checkout> record   # the record files only
 The GPU-side tests read only the outputs, never the reference tree.
 """
 
@@ -96,7 +97,9 @@ def record(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_fixtures.py <faber-runtime checkout> [record]")
+    root = sys.argv[1]
     if len(sys.argv) > 2 and sys.argv[2] == "record":
         record(root)
     else:

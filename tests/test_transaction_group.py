@@ -42,9 +42,16 @@ def _rank(rank, port, mode, q):
             if mode == "timeout" and rank == 1:
                 from faber_runtime_b200 import _lib
                 raise _lib.FaberError(_lib.TIMEOUT, "a tensor-parallel peer did not publish its partials in time")
+            if mode == "value_error" and rank == 1:
+                raise ValueError("TokenOutOfRange: token 99999 is outside the admitted vocab")
             return 1000 + rank
 
-        r = tx.run_group_step(t, b, ordinal=300, step=step, publish=published.append)
+        try:
+            r = tx.run_group_step(t, b, ordinal=300, step=step, publish=published.append)
+        except ValueError as e:  # raised again after this rank aborted
+            info = b.info()
+            q.put((rank, "raised", str(e), info["committed_bytes"], t.receipt().decision, published))
+            return
         q.put((rank, r.decision, r.published_bytes, b.info()["committed_bytes"], r.failure_kind, published))
     except Exception as e:  # reported, not hidden
         q.put((rank, "error", repr(e), 0, "", []))
@@ -89,6 +96,20 @@ def test_a_step_timeout_on_one_rank_aborts_every_rank():
     assert [o[1] for o in out] == ["Aborted"] * WORLD, out
     assert all(o[2] == 0 and o[5] == [] for o in out)  # nothing published, no token committed
     assert out[1][4] == "Cancelled"  # the step failed outside the backend: aborted with its reason
+
+
+def test_a_step_raising_a_foreign_error_still_votes_and_aborts_every_rank():
+    """A step that raises something other than a FaberError (here the
+    ValueError of a rejected token id) must not skip the group's vote: the
+    other rank aborts at once (not after the group's timeout), the failing
+    rank aborts too and then raises the error again."""
+    import time
+    t0 = time.monotonic()
+    out = _run("value_error")
+    assert time.monotonic() - t0 < 60  # well inside the 20 s group timeout plus start-up
+    assert out[0][1] == "Aborted" and out[0][2] == 0 and out[0][5] == []
+    assert out[1][1] == "raised" and "TokenOutOfRange" in out[1][2]
+    assert out[1][3] == 0 and out[1][4] == "Aborted" and out[1][5] == []
 
 
 def test_publish_runs_only_after_the_group_commits():

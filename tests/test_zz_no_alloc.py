@@ -7,12 +7,15 @@ cudaMalloc / cudaFree may synchronize the device. This entry point serves
 them: its scratch is a static device array inside the library, and the
 caller passes only inputs and outputs.
 
-The reference for the comparison is the existing session entry points, whose
-attention uses session-allocated scratch. A traced push over an installed
-K/V prefix gives that path's query, its new K/V row and its attention
-output; the static entry point gets the same query and cache rows. Two calls
-in a row must both agree, because the static scratch keeps the previous
-call's contents. The file is named to be collected last.
+Two comparators check its output. One is the existing session entry
+points, whose attention uses session-allocated scratch: a traced push over
+an installed K/V prefix gives that path's query, its new K/V row and its
+attention output, and the static entry point gets the same query and cache
+rows. The other is the CPU oracle's attention_gqa (src/cpu_oracle.rs:711-792)
+on the same f16-rounded rows. Two calls in a row must both agree, because
+the static scratch keeps the previous call's contents, and the calls must
+leave the device's free memory unchanged. The file is named to be collected
+last.
 """
 
 import numpy as np
@@ -64,13 +67,29 @@ def test_static_attention_matches_session_attention(cuda, heads, kv_heads, head_
     dq = torch.from_numpy(q).to(cuda)
     dk = torch.from_numpy(kc.astype(np.float16)).to(cuda)
     dv = torch.from_numpy(vc.astype(np.float16)).to(cuda)
+    # the oracle's attention over the same f16-rounded cache rows
+    import oracle as o
+    want = o.attention_gqa(q, kc.astype(np.float16).astype(np.float32),
+                           vc.astype(np.float16).astype(np.float32), 1, n_prefix + 1, heads,
+                           kv_heads, head_dim, 1.0 / np.sqrt(np.float32(head_dim)))
+    # every buffer exists before the first call, so nothing below allocates
+    # on the caller's side either
+    outs_dev = [torch.full((heads * head_dim,), float("nan"), dtype=torch.float32, device=cuda)
+                for _ in range(2)]
+    torch.cuda.synchronize()
     outs = []
-    for _ in range(2):
-        out = torch.full((heads * head_dim,), float("nan"), dtype=torch.float32, device=cuda)
+    for i, out in enumerate(outs_dev):
         static_attention(dq, dk, dv, out, heads, kv_heads, head_dim, n_prefix + 1)
         torch.cuda.synchronize()
+        if i == 0:  # after the first call: lazy module loading has happened
+            free0 = torch.cuda.mem_get_info()[0]
         outs.append(out.cpu().numpy())
         within(outs[-1], ref)
+        within(outs[-1], want)
+    for _ in range(3):
+        static_attention(dq, dk, dv, outs_dev[0], heads, kv_heads, head_dim, n_prefix + 1)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0, "a call changed the device's free memory"
     assert np.array_equal(outs[0], outs[1]), "two calls in a row differ"
     run.close()
     model.close()
@@ -85,6 +104,7 @@ def test_static_attention_rejects_sizes_beyond_its_scratch(cuda):
         (16, 4, 96, 10, "head_dim must be 64 or 128"),
         (32, 2, 128, 10, "more than 8 query heads"),
         (16, 4, 128, 0, "n_kv must be"),
+        (16, 4, 128, (1 << 31) - 32, "n_kv must be"),  # would overflow the 32-bit group count
     ]
     for heads, kv_heads, hd, n_kv, text in cases:
         with pytest.raises(FaberError) as e:
