@@ -127,6 +127,7 @@ SIGNATURES = {
     "faber_gpu_v2_q4k_upload": (Status, [P, U64, U64, U64, PP]),
     "faber_gpu_v2_q4k_free": (Status, [P]),
     "faber_gpu_v2_q4k_gemv": (Status, [P, P, P, P]),
+    "faber_gpu_v2_q4k_gemv_exchange": (Status, [P, P, P, ctypes.c_float, P, U32, U32, U32, P, P, P]),
     "faber_gpu_v2_q4k_dequant_rows": (Status, [P, P, I32, P]),
     "faber_gpu_v2_q4k_repack_hash": (Status, [P, ctypes.POINTER(U64)]),
     "faber_gpu_v2_kv_layout_bytes": (Status, [ctypes.POINTER(KvLayoutC), ctypes.POINTER(U64),
@@ -171,6 +172,9 @@ SIGNATURES = {
     "faber_gpu_v2_session_close": (Status, [P]),
     "faber_gpu_v2_session_reset": (Status, [P]),
     "faber_gpu_v2_session_len": (Status, [P, ctypes.POINTER(U64)]),
+    "faber_gpu_v2_session_truncate": (Status, [P, U64]),
+    "faber_gpu_v2_session_set_wait_limit": (Status, [P, U32]),
+    "faber_gpu_v2_session_exchange_epoch": (Status, [P, U32, ctypes.POINTER(U32)]),
     "faber_gpu_v2_session_push_token": (Status, [P, I64]),
     "faber_gpu_v2_session_push_tokens": (Status, [P, P, U64]),
     "faber_gpu_v2_session_step_greedy": (Status, [P, I64, P, U32, ctypes.POINTER(I64)]),

@@ -157,6 +157,8 @@ struct SessionState {
   int64_t* pinned = nullptr;  // pinned host staging
   size_t pinned_n = 0;
   uint64_t n = 0;         // host mirror of the sequence length
+  bool h_valid = false;   // h holds the residual stream of position n - 1
+  uint32_t peer_wait_limit = 0;  // polls before a tensor-parallel wait gives up (0: kernel default)
   bool prefix_pending = false;
   uint64_t prefix_n = 0;
   std::vector<uint8_t> prefix_layers;
@@ -715,6 +717,7 @@ inline void tp_consume_args(SessionState& S, GemvArgs& a, int which, uint32_t la
   a.epoch_ptr = &S.state.as<StepState>()->tp_epoch;
   a.red = S.tp_buf.as<unsigned long long>() + (size_t)which * tp * d;
   a.grid_bar = reinterpret_cast<unsigned int*>(S.tp_buf.as<unsigned long long>() + 2 * tp * d);
+  a.peer_wait_limit = S.peer_wait_limit;
 }
 
 inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV1& kv) {
@@ -961,6 +964,43 @@ inline void check_device_waits() {
               err == 2   ? "a tensor-parallel peer did not publish its partials in time"
               : err == 3 ? "a grid barrier wait expired"
                          : "a device pipeline wait expired");
+}
+
+// After a step whose device work failed (a bounded wait expired, or a
+// kernel-side token check), the device step state goes back to the length
+// the host held before the call, so the next push writes the same position
+// again. The failed step overwrote the residual stream, so the session needs
+// a push before its next logits. The exchange epoch is kept: every launched
+// step consumed one, and an epoch is never used twice.
+inline void rollback_step(SessionState& S, uint64_t n0) {
+  FABER_CUDA(cudaStreamSynchronize(S.stream));
+  StepState st;
+  FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+  st.n = (int32_t)n0;
+  st.cur_pos = n0 > 0 ? (int32_t)(n0 - 1) : 0;
+  st.status = 0;
+  st.argmax_key = 0ull;
+  FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
+  S.n = n0;
+  S.h_valid = false;
+}
+
+// Runs a step's device work; a TIMEOUT or KERNEL_ERROR rolls the step back.
+template <class F>
+inline void with_rollback(SessionState& S, F&& body) {
+  const uint64_t n0 = S.n;
+  try {
+    body();
+  } catch (const Error& e) {
+    if (e.code == FABER_STATUS_TIMEOUT || e.code == FABER_STATUS_KERNEL_ERROR) rollback_step(S, n0);
+    throw;
+  }
+}
+
+inline void require_residual(const SessionState& S) {
+  require(S.h_valid, FABER_STATUS_INVALID_ARGUMENT,
+          "the session has no residual for its last position (after an installed prefix, a failed "
+          "step or a truncation): push a token first");
 }
 
 inline cudaGraphExec_t capture(SessionState& S, const std::function<void()>& body) {
@@ -1216,9 +1256,11 @@ inline void run_push(SessionState& S, const int64_t* tokens, uint64_t count) {
                   std::to_string(M.cfg.vocab) + ")");
   require(S.n + count <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
   if (count == 0) return;
+  with_rollback(S, [&] {
   FABER_CUDA(cudaMemcpyAsync(S.prompt.p, tokens, count * 8, cudaMemcpyHostToDevice, S.stream));
   if (!S.trace && count >= kPrefillMinTokens && prefill_supported(M)) {
     run_prefill(S, S.prompt.as<int64_t>(), (int)count);
+    S.h_valid = true;
     return;
   }
   if (S.trace) {
@@ -1241,6 +1283,8 @@ inline void run_push(SessionState& S, const int64_t* tokens, uint64_t count) {
   FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
   require(st.status == 0, FABER_STATUS_KERNEL_ERROR, "device-side token check failed");
   S.n += count;
+  S.h_valid = true;
+  });
 }
 
 inline void gather_logits(SessionState& S, float* host, uint64_t cap) {
@@ -1261,6 +1305,7 @@ inline void run_position_logits(SessionState& S, float* host, uint64_t cap) {
   FABER_CUDA(cudaSetDevice(S.device));
   FABER_ARG(S.n > 0, "the session holds no tokens");
   FABER_ARG(host != nullptr, "null logits buffer");
+  require_residual(S);
   if (S.trace) {
     enqueue_logits(S, false, {});
   } else {
@@ -1281,7 +1326,9 @@ inline void run_greedy(SessionState& S, uint32_t n_gen, const int64_t* eog, uint
   if (n_gen == 0) return;
   require(S.n + n_gen - 1 <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
   check_prefix_complete(S);
+  require_residual(S);
   std::vector<int64_t> e(eog, eog + n_eog);
+  with_rollback(S, [&] {
   // reset the per-run counters
   StepState st;
   FABER_CUDA(cudaMemcpyAsync(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost, S.stream));
@@ -1310,6 +1357,8 @@ inline void run_greedy(SessionState& S, uint32_t n_gen, const int64_t* eog, uint
   if (!S.trace) FABER_CUDA(cudaEventElapsedTime(&S.last_greedy_ms, S.ev0, S.ev1));
   if (all_finite) *all_finite = st.finite;
   S.n += n_gen - 1;
+  S.h_valid = true;
+  });
   (void)M;
 }
 
@@ -1330,6 +1379,7 @@ inline int64_t run_step_greedy(SessionState& S, int64_t token, const int64_t* eo
   std::vector<int64_t> e(eog, eog + n_eog);
   StepState* st = st_ptr(S);
   int64_t* pin = static_cast<int64_t*>(S.pinned);
+  with_rollback(S, [&] {
   pin[0] = token;
   FABER_CUDA(cudaMemcpyAsync(&st->input_token, pin, 8, cudaMemcpyHostToDevice, S.stream));
   if (S.trace) {
@@ -1343,6 +1393,8 @@ inline int64_t run_step_greedy(SessionState& S, int64_t token, const int64_t* eo
   FABER_CUDA(cudaStreamSynchronize(S.stream));
   check_device_waits();
   S.n += 1;
+  S.h_valid = true;
+  });
   return pin[1];
 }
 
@@ -1622,6 +1674,7 @@ inline void run_batch_greedy(BatchState& Bt, uint32_t n_gen, const int64_t* eog,
     FABER_ARG(S.n > 0, "greedy decode needs a prompt in every session");
     require(S.n + n_gen - 1 <= (uint64_t)S.max_ctx, FABER_STATUS_IO_ERROR, "KV context is full");
     check_prefix_complete(S);
+    require_residual(S);
     // the session's own work has finished before the batch stream reads it
     FABER_CUDA(cudaStreamSynchronize(S.stream));
     StepState st;
@@ -1655,6 +1708,7 @@ inline void run_batch_greedy(BatchState& Bt, uint32_t n_gen, const int64_t* eog,
     if (all_finite) all_finite[i] = st.finite;
     for (uint32_t j = 0; j < n_gen; ++j) out[(size_t)i * n_gen + j] = gen[(size_t)i * Bt.gen_cap + j];
     S.n += n_gen - 1;
+    S.h_valid = true;
   }
 }
 
@@ -1681,6 +1735,7 @@ inline void set_prefix(SessionState& S, uint32_t layer, const float* k, const fl
   S.prefix_pending = true;
   S.prefix_n = n;
   S.n = n;
+  S.h_valid = false;
   StepState st;
   FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
   st.n = (int32_t)n;
@@ -1966,11 +2021,57 @@ FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_reset(FaberGpuSession* s) {
     st.tp_epoch = epoch;
     FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
     S.n = 0;
+    S.h_valid = false;
     S.prefix_pending = false;
     std::fill(S.prefix_layers.begin(), S.prefix_layers.end(), 0);
     S.c_position = 0;
     S.c_kv_generations = 0;
     S.c_history.clear();
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_truncate(FaberGpuSession* s, uint64_t n) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_truncate", [&] {
+    FABER_ARG(s, "null session");
+    SessionState& S = s->s;
+    FABER_ARG(n <= S.n, "truncate cannot lengthen the sequence (" + std::to_string(n) + " > " +
+                            std::to_string(S.n) + ")");
+    FABER_ARG(!S.prefix_pending || n >= S.prefix_n, "truncate cannot cut into an installed prefix");
+    if (n == S.n) return;
+    FABER_CUDA(cudaSetDevice(S.device));
+    rollback_step(S, n);
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_set_wait_limit(FaberGpuSession* s, uint32_t polls) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_set_wait_limit", [&] {
+    FABER_ARG(s, "null session");
+    SessionState& S = s->s;
+    if (S.peer_wait_limit == polls) return;
+    FABER_CUDA(cudaSetDevice(S.device));
+    FABER_CUDA(cudaStreamSynchronize(S.stream));
+    S.peer_wait_limit = polls;
+    S.destroy_graphs();  // the limit is a kernel argument: capture again
+  });
+}
+
+FABER_EXPORT FaberRtStatusV1 faber_gpu_v2_session_exchange_epoch(FaberGpuSession* s, uint32_t raise_to,
+                                                                uint32_t* epoch) {
+  using namespace faber;
+  return guarded("faber_gpu_v2_session_exchange_epoch", [&] {
+    FABER_ARG(s, "null session");
+    SessionState& S = s->s;
+    FABER_CUDA(cudaSetDevice(S.device));
+    FABER_CUDA(cudaStreamSynchronize(S.stream));
+    StepState st;
+    FABER_CUDA(cudaMemcpy(&st, S.state.p, sizeof(st), cudaMemcpyDeviceToHost));
+    if (raise_to > st.tp_epoch) {  // never lowered: an epoch is used once
+      st.tp_epoch = raise_to;
+      FABER_CUDA(cudaMemcpy(S.state.p, &st, sizeof(st), cudaMemcpyHostToDevice));
+    }
+    if (epoch) *epoch = st.tp_epoch;
   });
 }
 

@@ -604,6 +604,60 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_gemv(
   });
 }
 
+}  // extern "C"
+
+namespace faber {
+// Epoch base and grid-barrier words of the exchange validation call.
+__device__ uint32_t g_xcheck_epoch;
+__device__ unsigned int g_xcheck_bar[2];
+}  // namespace faber
+
+extern "C" {
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_gemv_exchange(
+    const FaberGpuQ4kTensor* t, const float* x, const float* norm_w, float eps, const uint64_t* exchange,
+    uint32_t tp, uint32_t epoch, uint32_t wait_limit, float* x_sum_out, float* y, void* stream) {
+  return guarded("faber_gpu_v2_q4k_gemv_exchange", [&] {
+    FABER_ARG(t && x && norm_w && exchange && x_sum_out && y, "null pointer");
+    FABER_ARG(tp >= 1 && tp <= (uint32_t)kMaxTp, "tp must be in [1, 8]");
+    FABER_ARG(epoch >= 1, "epoch 0 marks an empty exchange word");
+    const cudaStream_t st = as_stream(stream);
+    // a stale expiry flag of other work on this device is not this call's
+    int flag = 0;
+    FABER_CUDA(cudaStreamSynchronize(st));
+    FABER_CUDA(cudaMemcpyFromSymbol(&flag, g_pipe_error, sizeof(int)));
+    require(flag == 0, FABER_STATUS_TIMEOUT, "an earlier device wait on this device expired");
+    uint32_t* epoch_dev = nullptr;
+    unsigned int* bar_dev = nullptr;
+    FABER_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&epoch_dev), g_xcheck_epoch));
+    FABER_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&bar_dev), g_xcheck_bar));
+    const uint32_t base = epoch - 1u;  // the kernel's epoch: base * stages + stage + 1
+    FABER_CUDA(cudaMemcpyToSymbolAsync(g_xcheck_epoch, &base, sizeof(base), 0, cudaMemcpyHostToDevice, st));
+    GemvArgs a = t->t.args();
+    a.x = x;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.x_sum_out = x_sum_out;
+    a.out = y;
+    a.tp = (int32_t)tp;
+    a.tp_stage = 0;
+    a.tp_stages = 1;
+    a.epoch_ptr = epoch_dev;
+    a.red = reinterpret_cast<const unsigned long long*>(exchange);
+    a.grid_bar = bar_dev;
+    a.peer_wait_limit = wait_limit;
+    launch_gemv<WL_TILED, PRO_NORM_PEERS, EPI_STORE>(a, st, false);
+    FABER_CUDA(cudaStreamSynchronize(st));
+    FABER_CUDA(cudaMemcpyFromSymbol(&flag, g_pipe_error, sizeof(int)));
+    if (flag) {
+      const int zero = 0;
+      FABER_CUDA(cudaMemcpyToSymbol(g_pipe_error, &zero, sizeof(int)));
+      throw Error(FABER_STATUS_TIMEOUT, flag == 3 ? "a grid barrier wait expired"
+                                                  : "an exchange word did not carry the epoch in time");
+    }
+  });
+}
+
 __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_dequant_rows(
     const FaberGpuQ4kTensor* t, float* out, int32_t f16_round, void* stream) {
   return guarded("faber_gpu_v2_q4k_dequant_rows", [&] {

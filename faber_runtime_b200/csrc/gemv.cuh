@@ -96,6 +96,7 @@ struct GemvArgs {
   unsigned long long* peer_dst[kMaxTp];  // EPI_PEERS: this rank's slot in rank r's buffer
   const unsigned long long* red;       // PRO_NORM_PEERS: local buffer [tp][n_cols]
   unsigned int* grid_bar;              // PRO_NORM_PEERS: {arrived, generation} (local)
+  uint32_t peer_wait_limit;            // polls before a peer / grid-barrier wait gives up (0: default)
 };
 
 // Epoch of one exchange: unique per (step, exchange) and identical on every
@@ -120,13 +121,17 @@ __device__ __forceinline__ unsigned long long ld_peer(const unsigned long long* 
 // host reads and clears it after each step.
 __device__ int g_pipe_error;
 
-// One exchanged value once its epoch has arrived. Bounded: 2^20 polls (well
-// under a second), and no wait at all once an earlier wait has expired.
+// One exchanged value once its epoch has arrived. Bounded: by default 2^20
+// polls (well under a second; a session can set a shorter limit), and no
+// wait at all once an earlier wait has expired.
 constexpr uint32_t kPeerSpinLimit = 1u << 20;
-__device__ __forceinline__ float peer_value(const unsigned long long* p, uint32_t epoch) {
+__device__ __forceinline__ uint32_t peer_limit(const GemvArgs& a) {
+  return a.peer_wait_limit ? a.peer_wait_limit : kPeerSpinLimit;
+}
+__device__ __forceinline__ float peer_value(const unsigned long long* p, uint32_t epoch, uint32_t limit) {
   unsigned long long w = ld_peer(p);
   for (uint32_t n = 0; (uint32_t)(w >> 32) != epoch; w = ld_peer(p)) {
-    if (++n == kPeerSpinLimit || ((n & 1023u) == 0 && *(volatile int*)&g_pipe_error)) {
+    if (++n >= limit || ((n & 1023u) == 0 && *(volatile int*)&g_pipe_error)) {
       atomicExch(&g_pipe_error, 2);
       break;
     }
@@ -146,8 +151,9 @@ __device__ __forceinline__ float peer_sum1(const GemvArgs& a, int i, uint32_t e)
 #pragma unroll
   for (int p = 0; p < kMaxTp; ++p) {
     if (p >= a.tp) break;
-    const float v = (uint32_t)(w[p] >> 32) == e ? __uint_as_float((uint32_t)w[p])
-                                                : peer_value(a.red + (size_t)p * a.n_cols + i, e);
+    const float v = (uint32_t)(w[p] >> 32) == e
+                        ? __uint_as_float((uint32_t)w[p])
+                        : peer_value(a.red + (size_t)p * a.n_cols + i, e, peer_limit(a));
     s = p == 0 ? v : s + v;
   }
   return s;
@@ -155,8 +161,8 @@ __device__ __forceinline__ float peer_sum1(const GemvArgs& a, int i, uint32_t e)
 
 // Grid-wide barrier of a persistent grid (every CTA resident), thread 0 of
 // each CTA; sense-reversing, so the same two words serve every launch.
-// Bounded like the other waits.
-__device__ __forceinline__ void grid_barrier(unsigned int* bar) {
+// Bounded like the peer waits.
+__device__ __forceinline__ void grid_barrier(unsigned int* bar, uint32_t limit) {
   volatile unsigned int* gen = bar + 1;
   const unsigned int my_gen = *gen;
   __threadfence();
@@ -167,7 +173,7 @@ __device__ __forceinline__ void grid_barrier(unsigned int* bar) {
     return;
   }
   for (uint32_t n = 0; *gen == my_gen; ++n) {
-    if (n == kPeerSpinLimit) {
+    if (n >= limit) {
       atomicExch(&g_pipe_error, 3);
       break;
     }
@@ -298,7 +304,7 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
     for (int i = (int)blockIdx.x * per + tid; i < i1; i += NT)
       a.x_sum_out[i] = a.x[i] + peer_sum1(a, i, e);
     cbar<NAMED>();
-    if (tid == 0) grid_barrier(a.grid_bar);
+    if (tid == 0) grid_barrier(a.grid_bar, peer_limit(a));
     cbar<NAMED>();
   }
   const bool vec = (n % 4 == 0) && aligned16(a.x) &&

@@ -188,6 +188,23 @@ class ForwardRun:
     def reset(self) -> None:
         _lib.call("faber_gpu_v2_session_reset", self._h)
 
+    def truncate(self, n: int) -> None:
+        """Shorten the sequence to ``n`` positions (the rollback of a step whose
+        group aborted); the next call must be a push."""
+        _lib.call("faber_gpu_v2_session_truncate", self._h, int(n))
+
+    def set_wait_limit(self, polls: int) -> None:
+        """Polls before a tensor-parallel peer or grid-barrier wait gives up
+        and the step fails with TIMEOUT (0: the kernels' default)."""
+        _lib.call("faber_gpu_v2_session_set_wait_limit", self._h, int(polls))
+
+    def exchange_epoch(self, raise_to: int = 0) -> int:
+        """The tensor-parallel exchange epoch, after raising it to
+        ``raise_to`` if that is larger (it is never lowered)."""
+        e = _lib.U32()
+        _lib.call("faber_gpu_v2_session_exchange_epoch", self._h, int(raise_to), ctypes.byref(e))
+        return e.value
+
     def commit(self, token: int, position: int, kv_generation: int,
                publication_boundary: int = 1) -> str:
         """SequenceState::commit: returns "applied" or "idempotent_replay"."""

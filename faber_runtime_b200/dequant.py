@@ -57,6 +57,15 @@ class Q4kTensor:
     def dequant_rows(self, out_ptr: int, f16_round: bool = True, stream: int = 0) -> None:
         _lib.call("faber_gpu_v2_q4k_dequant_rows", self._h, out_ptr, int(f16_round), stream)
 
+    def gemv_exchange(self, x_ptr: int, norm_w_ptr: int, eps: float, exchange_ptr: int, tp: int,
+                      epoch: int, wait_limit: int, x_sum_ptr: int, y_ptr: int, stream: int = 0) -> None:
+        """The exchange-consuming GEMV of a tensor-parallel step on local
+        buffers: x_sum = x + the tp partial rows of ``exchange`` whose words
+        carry ``epoch``; y = dense(w, rms_norm(x_sum) * norm_w). Raises
+        FaberError(TIMEOUT) when a word never carries the epoch."""
+        _lib.call("faber_gpu_v2_q4k_gemv_exchange", self._h, x_ptr, norm_w_ptr, float(eps), exchange_ptr,
+                  int(tp), int(epoch), int(wait_limit), x_sum_ptr, y_ptr, stream)
+
     def repack_hash(self) -> int:
         v = _lib.U64()
         _lib.call("faber_gpu_v2_q4k_repack_hash", self._h, ctypes.byref(v))

@@ -272,8 +272,24 @@ def admitted(transfer_staging_bytes: int, activation_scratch_bytes: int, **class
                            activation_scratch_bytes=activation_scratch_bytes, **classes)
 
 
+def realign_after_abort(session, length: int, group=None) -> None:
+    """Put a tensor-parallel session back where the group agreed after an
+    aborted step: the sequence is truncated to ``length`` (on a rank whose
+    step ran; a rank whose step failed was rolled back by the call itself),
+    and every rank raises its exchange epoch to the largest in the group, so
+    that the next step's exchanges match on every rank again and no epoch
+    is used twice. Every rank of the group must call it."""
+    import torch
+    import torch.distributed as dist
+    if len(session) > length:
+        session.truncate(length)
+    e = torch.tensor([session.exchange_epoch()], dtype=torch.int64)
+    dist.all_reduce(e, op=dist.ReduceOp.MAX, group=group)
+    session.exchange_epoch(int(e.item()))
+
+
 def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=None, step=None,
-                   publish=None) -> Receipt:
+                   publish=None, session=None) -> Receipt:
     """Execute this rank's transaction, then agree with every rank of the
     process group on the outcome before anything is published: commit only
     when every rank executed its step, abort everywhere otherwise.
@@ -295,10 +311,14 @@ def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=No
     The device state is not rolled back: on a rank whose step ran, the
     session has already written that position's K/V rows and advanced its
     length, so after an abort the caller resets the session and replays its
-    committed tokens before the next step."""
+    committed tokens before the next step. Given the rank's ``session`` (a
+    ForwardRun of the group's model), an abort instead truncates it back to
+    the length it had before the step and realigns the group's exchange
+    epochs (``realign_after_abort``), so the step can simply be retried."""
     import torch
     import torch.distributed as dist
     reason, result, foreign = "", None, None
+    length = len(session) if session is not None else 0
     try:
         t.execute(backend)
         if step is not None:
@@ -322,6 +342,12 @@ def run_group_step(t: Transaction, backend: FaultBackend, ordinal: int, group=No
             publish(result)
         return receipt
     receipt = t.abort(backend, reason or "another rank failed")
+    if session is not None:
+        try:
+            realign_after_abort(session, length, group)
+        except Exception:  # noqa: BLE001 - a group that failed cannot realign
+            if len(session) > length:
+                session.truncate(length)
     if foreign is not None:
         raise foreign
     return receipt

@@ -164,6 +164,19 @@ FaberRtStatusV1 faber_gpu_v2_q4k_free(FaberGpuQ4kTensor* t);
 /* y = dense(w, x) with the resident weight (x, y device pointers). */
 FaberRtStatusV1 faber_gpu_v2_q4k_gemv(const FaberGpuQ4kTensor* t, const float* x, float* y,
                                       void* stream);
+/* Validation surface of the tensor-parallel exchange (the row-parallel
+ * all-reduce of src/partition.rs's plan, fused into the next GEMV): with
+ * the resident weight, x_sum = x + sum over r < tp of exchange[r] (rank
+ * order) and y = dense(w, rms_norm(x_sum) * norm_w), where exchange is a
+ * device array [tp][cols] of 8-byte words (epoch << 32 | f32 bits) and a
+ * word counts only once it carries `epoch`. A word that never does makes the
+ * kernel's bounded wait give up after wait_limit polls (0: the default): the
+ * call then returns TIMEOUT and the device stays usable. Synchronizes
+ * `stream`; calls must not overlap (they share two device words). */
+FaberRtStatusV1 faber_gpu_v2_q4k_gemv_exchange(const FaberGpuQ4kTensor* t, const float* x,
+                                               const float* norm_w, float eps, const uint64_t* exchange,
+                                               uint32_t tp, uint32_t epoch, uint32_t wait_limit,
+                                               float* x_sum_out, float* y, void* stream);
 /* Dequantize the resident (repacked) weight back to [rows][cols] f32 —
  * proves the repack is value-identical to dequant_tensor. */
 FaberRtStatusV1 faber_gpu_v2_q4k_dequant_rows(const FaberGpuQ4kTensor* t, float* out,
@@ -437,6 +450,26 @@ FaberRtStatusV1 faber_gpu_v2_session_close(FaberGpuSession* s);
 /* Forget every position (a new sequence epoch; weights stay resident). */
 FaberRtStatusV1 faber_gpu_v2_session_reset(FaberGpuSession* s);
 FaberRtStatusV1 faber_gpu_v2_session_len(const FaberGpuSession* s, uint64_t* n);
+/* Shorten the sequence to n positions (n <= the current length, not into an
+ * installed prefix): the one-position rollback of a step whose group
+ * aborted (src/execution_transaction/transaction.rs:427-488 pairs an abort
+ * with no token commit, src/session.rs:422-456). The K/V rows past n stay
+ * in memory and are overwritten by the next pushes; the session needs a
+ * push before its next logits. A step whose device work fails with TIMEOUT
+ * or KERNEL_ERROR is rolled back the same way by the call itself. */
+FaberRtStatusV1 faber_gpu_v2_session_truncate(FaberGpuSession* s, uint64_t n);
+/* Polls before a tensor-parallel peer wait or grid-barrier wait of this
+ * session's kernels gives up and the step returns TIMEOUT (0: the default,
+ * 2^20 polls, well under a second). Mirrors the bounded waits behind
+ * BackendError::Timeout (src/execution_transaction/backend.rs:17-54). */
+FaberRtStatusV1 faber_gpu_v2_session_set_wait_limit(FaberGpuSession* s, uint32_t polls);
+/* The session's tensor-parallel exchange epoch (one per launched step): the
+ * current value in *epoch, after raising it to raise_to when that is
+ * larger (never lowered, so no epoch is used twice). After a group abort
+ * the ranks raise every session to the largest epoch of the group, so that
+ * their next exchanges match again. */
+FaberRtStatusV1 faber_gpu_v2_session_exchange_epoch(FaberGpuSession* s, uint32_t raise_to,
+                                                    uint32_t* epoch);
 /* ForwardRun::push_token (src/cpu_oracle.rs:859-912): append one token.
  * A token outside [0, vocab) or a full context is INVALID_ARGUMENT / IO_ERROR
  * and leaves the session unchanged. */

@@ -38,7 +38,32 @@ def _rank(rank, port, mode, q):
             os._exit(3)  # gone before the decision, nothing in flight
         published = []
 
-        def step():  # this rank's device work; rank 1's exchange wait expires in "timeout"
+        class FakeSession:  # the length / truncate / epoch surface of a ForwardRun
+            def __init__(self):
+                self.n, self.epoch, self.calls = 40, 100 + rank, []
+
+            def __len__(self):
+                return self.n
+
+            def truncate(self, n):
+                self.calls.append(("truncate", n))
+                self.n = n
+
+            def exchange_epoch(self, raise_to=0):
+                self.epoch = max(self.epoch, raise_to)
+                return self.epoch
+
+        sess = FakeSession() if mode == "session" else None
+
+        def step():
+            if sess is not None:  # rank 0's step ran (length advanced); rank 1's failed
+                if rank == 1:
+                    from faber_runtime_b200 import _lib
+                    raise _lib.FaberError(_lib.TIMEOUT, "exchange wait expired")
+                sess.n += 1
+                sess.epoch += 1
+                return 1000 + rank
+            # this rank's device work; rank 1's exchange wait expires in "timeout"
             if mode == "timeout" and rank == 1:
                 from faber_runtime_b200 import _lib
                 raise _lib.FaberError(_lib.TIMEOUT, "a tensor-parallel peer did not publish its partials in time")
@@ -47,11 +72,13 @@ def _rank(rank, port, mode, q):
             return 1000 + rank
 
         try:
-            r = tx.run_group_step(t, b, ordinal=300, step=step, publish=published.append)
+            r = tx.run_group_step(t, b, ordinal=300, step=step, publish=published.append, session=sess)
         except ValueError as e:  # raised again after this rank aborted
             info = b.info()
             q.put((rank, "raised", str(e), info["committed_bytes"], t.receipt().decision, published))
             return
+        if sess is not None:
+            published = [len(sess), sess.epoch, sess.calls]
         q.put((rank, r.decision, r.published_bytes, b.info()["committed_bytes"], r.failure_kind, published))
     except Exception as e:  # reported, not hidden
         q.put((rank, "error", repr(e), 0, "", []))
@@ -121,3 +148,15 @@ def test_a_rank_that_dies_aborts_the_survivor():
     out = _run("dies")
     assert len(out) == 1 and out[0][0] == 0
     assert out[0][1] == "Aborted" and out[0][2] == 0, out
+
+
+def test_an_abort_truncates_the_session_and_realigns_the_exchange_epochs():
+    """With the rank's session given, an aborted step leaves every rank at
+    the length it had before the step and at the group's largest exchange
+    epoch, so the step can be retried."""
+    out = _run("session")
+    assert [o[1] for o in out] == ["Aborted"] * WORLD, out
+    (n0, e0, c0), (n1, e1, c1) = out[0][5], out[1][5]
+    assert n0 == n1 == 40
+    assert e0 == e1 == 101  # rank 0 advanced 100 -> 101; rank 1 raised from 101
+    assert c0 == [("truncate", 40)] and c1 == []
