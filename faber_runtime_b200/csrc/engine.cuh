@@ -350,6 +350,8 @@ inline SessionSizes session_sizes(const FaberModelConfigV1& c, int Hl, int Hkvl,
   z.state = sizeof(StepState);
   z.gen = ctx * 8 + 8;
   z.prompt = ctx * 8;
+  // partials [2][tp][d], then 256 bytes: the grid-barrier words, and from
+  // byte 64 the argmax exchange [tp][3] (key high, key low, finite flag)
   z.tp_buf = tp > 1 ? 2 * tp * d * sizeof(unsigned long long) + 256 : 0;
   return z;
 }
@@ -694,13 +696,23 @@ inline void open_tp_exchange(SessionState& S) {
   }
 }
 
+// Exchanges per step: O and down of every layer, then the argmax.
+inline int tp_stages(const ModelState& M) { return (int)(2 * M.cfg.n_layers) + 1; }
+
+// The argmax exchange words of a rank's buffer: [tp][3] u64 from byte 64 of
+// the 256-byte tail after the partials.
+inline unsigned long long* tp_argmax_words(const SessionState& S, unsigned char* base) {
+  const ModelState& M = S.m->s;
+  return reinterpret_cast<unsigned long long*>(base + 2 * (size_t)M.tp * M.cfg.d_model * 8 + 64);
+}
+
 // Producer side of exchange `which` (0: O, 1: down) of `layer`.
 inline void tp_publish_args(SessionState& S, GemvArgs& a, int which, uint32_t layer) {
   ModelState& M = S.m->s;
   const size_t tp = (size_t)M.tp, d = M.cfg.d_model;
   a.tp = M.tp;
   a.tp_stage = (int)(2 * layer) + which;
-  a.tp_stages = (int)(2 * M.cfg.n_layers);
+  a.tp_stages = tp_stages(M);
   a.epoch_ptr = &S.state.as<StepState>()->tp_epoch;
   for (size_t r = 0; r < tp; ++r)
     a.peer_dst[r] = reinterpret_cast<unsigned long long*>(S.tp_base[r]) +
@@ -713,7 +725,7 @@ inline void tp_consume_args(SessionState& S, GemvArgs& a, int which, uint32_t la
   const size_t tp = (size_t)M.tp, d = M.cfg.d_model;
   a.tp = M.tp;
   a.tp_stage = (int)(2 * layer) + which;
-  a.tp_stages = (int)(2 * M.cfg.n_layers);
+  a.tp_stages = tp_stages(M);
   a.epoch_ptr = &S.state.as<StepState>()->tp_epoch;
   a.red = S.tp_buf.as<unsigned long long>() + (size_t)which * tp * d;
   a.grid_bar = reinterpret_cast<unsigned int*>(S.tp_buf.as<unsigned long long>() + 2 * tp * d);
@@ -782,6 +794,59 @@ inline void session_open(SessionState& S, FaberGpuModel* m, const FaberKvLayoutV
 }
 
 inline StepState* st_ptr(SessionState& S) { return S.state.as<StepState>(); }
+
+// The argmax of a tensor-parallel step: every rank holds the best key of its
+// vocab shard (ordered value, then inverted id, so the lowest id wins ties,
+// src/cpu_oracle.rs:979-995) and its finite flag. Each rank stores them with
+// the step's epoch into its slot of every rank's exchange words (8-byte
+// single-copy-atomic stores), then takes the maximum key and the minimum
+// flag over all ranks' words once they carry the epoch, in rank order, and
+// finishes the step like finalize_kernel. Waits are bounded (TIMEOUT).
+struct ArgmaxPeers {
+  unsigned long long* dst[kMaxTp];  // this rank's slot in rank r's words
+  const unsigned long long* src;    // this rank's words [tp][3]
+  const uint32_t* epoch_ptr;
+  int32_t tp, stage, stages;
+  uint32_t limit;                   // polls (0: the default)
+};
+
+__global__ void finalize_tp_kernel(StepState* st, int64_t* gen, int32_t gen_cap, const ArgmaxPeers x) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t e = *x.epoch_ptr * (uint32_t)x.stages + (uint32_t)x.stage + 1u;
+  const unsigned long long mine = st->argmax_key;
+  const uint32_t fin = st->finite ? 1u : 0u;
+  const int lane = threadIdx.x;
+  if (lane < x.tp) {
+    unsigned long long* d = x.dst[lane];
+    st_peer(d + 0, __uint_as_float((uint32_t)(mine >> 32)), e);
+    st_peer(d + 1, __uint_as_float((uint32_t)mine), e);
+    st_peer(d + 2, __uint_as_float(fin), e);
+  }
+  __syncwarp();
+  if (lane != 0) return;
+  const uint32_t limit = x.limit ? x.limit : kPeerSpinLimit;
+  unsigned long long best = 0ull;
+  uint32_t all_fin = 1u;
+  for (int p = 0; p < x.tp; ++p) {
+    const unsigned long long* w = x.src + 3 * p;
+    const uint32_t hi = __float_as_uint(peer_value(w + 0, e, limit));
+    const uint32_t lo = __float_as_uint(peer_value(w + 1, e, limit));
+    const uint32_t f = __float_as_uint(peer_value(w + 2, e, limit));
+    const unsigned long long k = ((unsigned long long)hi << 32) | lo;
+    best = k > best ? k : best;
+    all_fin &= f;
+  }
+  st->finite = (int32_t)all_fin;
+  const int64_t tok = best ? (int64_t)(0xffffffffu - (uint32_t)(best & 0xffffffffull)) : 0;
+  st->input_token = tok;
+  const int32_t c = st->gen_count;
+  if (gen && c >= 0 && c < gen_cap) {
+    gen[c] = tok;
+    st->gen_count = c + 1;
+  }
+  st->argmax_key = 0ull;
+}
 
 // Enqueue one push step (embedding + all layers) on S.stream.
 inline void enqueue_push(SessionState& S, bool pdl) {
@@ -945,11 +1010,22 @@ inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>
     else launch_gemv<WL_TILED, PRO_NORM, EPI_LOGITS>(a, S.stream, pdl);
   }
   if (M.tp > 1) {
-    FABER_NCCL(ncclAllReduce(&st->argmax_key, &st->argmax_key, 1, ncclUint64, ncclMax, M.comm, S.stream));
-    FABER_NCCL(ncclAllReduce(&st->finite, &st->finite, 1, ncclInt32, ncclMin, M.comm, S.stream));
+    // the group's argmax and finite flag through peer memory: no collective
+    // on the token path, bounded waits like the other exchanges
+    ArgmaxPeers x = {};
+    for (int r = 0; r < M.tp; ++r) x.dst[r] = tp_argmax_words(S, S.tp_base[r]) + 3 * M.rank;
+    x.src = tp_argmax_words(S, S.tp_buf.as<unsigned char>());
+    x.epoch_ptr = &st->tp_epoch;
+    x.tp = M.tp;
+    x.stage = 2 * (int)c.n_layers;
+    x.stages = tp_stages(M);
+    x.limit = S.peer_wait_limit;
+    launch_pdl(finalize_tp_kernel, dim3(1), dim3(32), 0, S.stream, pdl, st, S.gen.as<int64_t>(),
+               (int32_t)S.max_ctx, x);
+  } else {
+    launch_pdl(finalize_kernel, dim3(1), dim3(1), 0, S.stream, pdl, st, S.gen.as<int64_t>(),
+               (int32_t)S.max_ctx);
   }
-  launch_pdl(finalize_kernel, dim3(1), dim3(1), 0, S.stream, pdl && M.tp == 1, st, S.gen.as<int64_t>(),
-             (int32_t)S.max_ctx);
 }
 
 // A device-side bounded wait that expired (pipeline stage or tensor-parallel

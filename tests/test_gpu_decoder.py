@@ -247,6 +247,34 @@ def test_prompt_pass_matches_oracle(cuda, which, n_prompt):
     assert fin and toks.tolist() == ref_tokens.tolist()
 
 
+def test_prompt_pass_2048_tokens_7b_width_matches_incremental_decode(cuda):
+    """The benchmark's prompt pass (2048 ids, 7B width, one chunk of tcgen05
+    GEMMs and tensor-core flash attention) against the same prompt pushed
+    one token at a time through the decode path, which the oracle tests pin
+    (an oracle prompt pass over 2048 7B-width positions takes CPU-hours):
+    the last position's logits within 1e-3 x RMS, the same argmax, and the
+    same greedy continuation over the two caches."""
+    from faber_runtime_b200 import LLAMA2_7B, DeviceModel, ForwardRun, synth
+    cfg = LLAMA2_7B.with_layers(2)
+    dm = DeviceModel(cfg, synth.model_tensors(cfg, 93, norms="random"))
+    prompt = synth.tokens(93, 4, 2048, cfg.vocab)
+    fast = ForwardRun(dm, context_length=2048 + 8)
+    fast.push_tokens(prompt)  # one prompt-pass chunk
+    slow = ForwardRun(dm, context_length=2048 + 8)
+    for t in prompt:
+        slow.push_token(int(t))  # the decode step, token by token
+    assert len(fast) == len(slow) == 2048
+    a, b = fast.position_logits(), slow.position_logits()
+    within(a, b)
+    assert int(np.argmax(a)) == int(np.argmax(b))
+    ta, fa = fast.greedy(4)
+    tb, fb = slow.greedy(4)
+    assert fa and fb and ta.tolist() == tb.tolist()
+    fast.close()
+    slow.close()
+    dm.close()
+
+
 def test_reset_session_reruns_prompt_pass_identically(cuda):
     """A session reset and the same prompt pushed again through the prompt
     pass gives bit-identical
