@@ -466,7 +466,7 @@ def batch_legs(cfg, model, args):
              "linear_tflops_useful": flop / pf_s / 1e12, "path": "tensor-core prompt pass per sequence"},
             {"sequences": 16, "steps": args.steps, "ms_per_step": ms / args.steps,
              "tok_s": 16 * args.steps / (ms * 1e-3), "all_finite": bool(fin.all()),
-             "path": "batched tcgen05 Q4_K GEMMs, per-sequence attention",
+             "path": "batched Q4_K GEMV (one weight formation for all 16 sequences), per-sequence attention",
              "context": f"{PREFILL} + up to {args.warmup + args.steps}"})
 
 

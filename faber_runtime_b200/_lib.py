@@ -128,6 +128,7 @@ SIGNATURES = {
     "faber_gpu_v2_q4k_free": (Status, [P]),
     "faber_gpu_v2_q4k_gemv": (Status, [P, P, P, P]),
     "faber_gpu_v2_q4k_gemv_exchange": (Status, [P, P, P, ctypes.c_float, P, U32, U32, U32, P, P, P]),
+    "faber_gpu_v2_q4k_gemv_batch": (Status, [P, P, U32, P, P]),
     "faber_gpu_v2_q4k_dequant_rows": (Status, [P, P, I32, P]),
     "faber_gpu_v2_q4k_repack_hash": (Status, [P, ctypes.POINTER(U64)]),
     "faber_gpu_v2_kv_layout_bytes": (Status, [ctypes.POINTER(KvLayoutC), ctypes.POINTER(U64),

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "bgemv.cuh"
 #include "prefill.cuh"
 
 namespace faber {
@@ -1527,6 +1528,58 @@ inline bool batch_supported(const ModelState& M) {
   return prefill_supported(M) && !M.cfg.tied_head && M.head.identity;
 }
 
+// K slabs of a batched GEMV over W for B sequences.
+inline int bgemv_slabs(const DeviceTiled& W, int B) {
+  const int sb = bg_slab_sb(W.nb, B);
+  return (W.nb + sb - 1) / sb;
+}
+
+// Partial-sum scratch (floats) and tile tickets a batched GEMV over W needs.
+inline size_t bgemv_part_floats(const DeviceTiled& W, int B) {
+  const int ns = bgemv_slabs(W, B);
+  return ns > 1 ? (size_t)ns * W.n_tiles * kTileRows * B : 0;
+}
+
+// One instantiation per (epilogue, column blocks): each sets its own
+// shared-memory opt-in once per device.
+template <int EPI, int NB>
+void launch_bgemv_nb(const BgemvArgs& a, int grid, size_t smem, cudaStream_t stream) {
+  auto kern = bgemv_kernel<EPI, NB>;
+  static thread_local std::map<int, bool> attr_done;
+  int dev = 0;
+  FABER_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBgSmemMax));
+    attr_done[dev] = true;
+  }
+  kern<<<grid, kPipeThreads, smem, stream>>>(a);
+  FABER_CUDA(cudaGetLastError());
+}
+
+template <int EPI>
+void launch_bgemv(const DeviceTiled& W, BgemvArgs a, int B, int K, cudaStream_t stream) {
+  require(W.identity, FABER_STATUS_UNSUPPORTED, "batched GEMV needs rows in whole super-blocks");
+  require(B >= 1 && B <= kBgMaxSeq, FABER_STATUS_INVALID_ARGUMENT, "batched GEMV takes 1 to 16 sequences");
+  a.w = W.w.as<uint8_t>();
+  a.n_tiles = W.n_tiles;
+  a.nb = W.nb;
+  a.n_rows = W.rows;
+  a.B = B;
+  a.K = K;
+  a.slab_sb = bg_slab_sb(W.nb, B);
+  a.n_slabs = (W.nb + a.slab_sb - 1) / a.slab_sb;
+  const BgLayout L = bg_layout(a.slab_sb, B);
+  require(L.total <= kBgSmemMax, FABER_STATUS_UNSUPPORTED, "batched GEMV slab exceeds shared memory");
+  const int grid = std::max(a.n_slabs, device_info().sms);
+  if (B <= 4) launch_bgemv_nb<EPI, 1>(a, grid, L.total, stream);
+  else if (B <= 8) launch_bgemv_nb<EPI, 2>(a, grid, L.total, stream);
+  else launch_bgemv_nb<EPI, 4>(a, grid, L.total, stream);
+  if (a.n_slabs > 1) {
+    bg_combine_kernel<EPI><<<(a.n_tiles + kBgCombineWarps - 1) / kBgCombineWarps, kBgCombineWarps * 32, 0, stream>>>(a);
+    FABER_CUDA(cudaGetLastError());
+  }
+}
+
 inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   FABER_ARG(n >= 1 && n <= kBatchMax, "a batch holds 1 to " + std::to_string(kBatchMax) + " sessions");
   SessionState& S0 = *seqs[0];
@@ -1591,6 +1644,21 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
     need(L.down);
   }
   need(M.head);
+  // the batched GEMV's slab partials and tickets
+  size_t bpart = 0, btiles = 0;
+  auto bneed = [&](const DeviceTiled& W) {
+    bpart = std::max(bpart, bgemv_part_floats(W, n));
+    btiles = std::max(btiles, (size_t)W.n_tiles);
+  };
+  for (const LayerDev& L : M.layers) {
+    bneed(L.qkv);
+    bneed(L.o);
+    bneed(L.gateup);
+    bneed(L.down);
+  }
+  bneed(M.head);
+  part = std::max(part, bpart);
+  tiles = std::max(tiles, btiles);
   Bt.kpart.alloc(std::max<size_t>(part, 1) * 4);
   Bt.tile_cnt.alloc(tiles * 4);
   FABER_CUDA(cudaMemset(Bt.tile_cnt.p, 0, Bt.tile_cnt.n));
@@ -1606,7 +1674,8 @@ inline void enqueue_batch_logits(BatchState& Bt, const std::vector<int64_t>& eog
   __half* xs = Bt.xs.as<__half>();
   prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.h.as<float>(), d, M.out_norm.as<float>(),
                                                                  c.rms_eps, xs, Bt.xscale.as<float>());
-  PrefillGemmArgs a = {};
+  BgemvArgs a = {};
+  a.xs = xs;
   a.xscale = Bt.xscale.as<float>();
   a.out = Bt.logits.as<float>();
   a.ld_out = (int)c.vocab;
@@ -1614,9 +1683,7 @@ inline void enqueue_batch_logits(BatchState& Bt, const std::vector<int64_t>& eog
   a.n_eog = (int)eog.size();
   for (size_t i = 0; i < eog.size(); ++i) a.eog[i] = eog[i];
   a.part = Bt.kpart.as<float>();
-  a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
-  launch_prefill_gemm<PG_LOGITS, kPgBNSlots>(M.head, xs_tensor_map(xs, kPgBNSlots, d, kPgBNSlots), a, n,
-                                             Bt.stream, batch_k_splits(M.head));
+  launch_bgemv<BG_LOGITS>(M.head, a, n, d, Bt.stream);
   slots_finalize_kernel<<<n, 32, 0, Bt.stream>>>(sl0, Bt.gen.as<int64_t>(), Bt.gen_cap);
   FABER_CUDA(cudaGetLastError());
 }
@@ -1632,9 +1699,6 @@ inline void enqueue_batch_push(BatchState& Bt) {
   float* H = Bt.h.as<float>();
   __half* xs = Bt.xs.as<__half>();
   float* xscale = Bt.xscale.as<float>();
-  const CUtensorMap map_d = xs_tensor_map(xs, kPgBNSlots, d, kPgBNSlots);
-  const CUtensorMap map_q = xs_tensor_map(xs, kPgBNSlots, nq, kPgBNSlots);
-  const CUtensorMap map_f = xs_tensor_map(xs, kPgBNSlots, F, kPgBNSlots);
   slots_embed_kernel<<<n, 256, 0, Bt.stream>>>(sl, M.embd_f16.as<__half>(), d, (int)c.vocab, H);
   FABER_CUDA(cudaGetLastError());
   for (uint32_t l = 0; l < c.n_layers; ++l) {
@@ -1643,7 +1707,8 @@ inline void enqueue_batch_push(BatchState& Bt) {
     prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(H, d, L.attn_norm.as<float>(), c.rms_eps,
                                                                    xs, xscale);
     {
-      PrefillGemmArgs a = {};
+      BgemvArgs a = {};
+      a.xs = xs;
       a.xscale = xscale;
       a.q_out = Bt.q.as<float>();
       a.rope = S0.rope.as<float2>();
@@ -1652,8 +1717,7 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.head_dim = hd;
       a.slots = sll;
       a.part = Bt.kpart.as<float>();
-      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
-      launch_prefill_gemm<PG_QKV_SLOTS, kPgBNSlots>(L.qkv, map_d, a, n, Bt.stream, batch_k_splits(L.qkv));
+      launch_bgemv<BG_QKV>(L.qkv, a, n, d, Bt.stream);
     }
     {
       AttnArgs a = {};
@@ -1679,35 +1743,35 @@ inline void enqueue_batch_push(BatchState& Bt) {
     prefill_split_kernel<false><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.ctx.as<float>(), nq, nullptr, 0.0f,
                                                                     xs, xscale);
     {
-      PrefillGemmArgs a = {};
+      BgemvArgs a = {};
+      a.xs = xs;
       a.xscale = xscale;
       a.out = H;
       a.ld_out = d;
       a.part = Bt.kpart.as<float>();
-      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
-      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.o, map_q, a, n, Bt.stream, batch_k_splits(L.o));
+      launch_bgemv<BG_RESID>(L.o, a, n, nq, Bt.stream);
     }
     prefill_split_kernel<true><<<n, kGemvThreads, 0, Bt.stream>>>(H, d, L.ffn_norm.as<float>(), c.rms_eps,
                                                                    xs, xscale);
     {
-      PrefillGemmArgs a = {};
+      BgemvArgs a = {};
+      a.xs = xs;
       a.xscale = xscale;
       a.out = Bt.act.as<float>();
       a.ld_out = F;
       a.part = Bt.kpart.as<float>();
-      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
-      launch_prefill_gemm<PG_SWIGLU, kPgBNSlots>(L.gateup, map_d, a, n, Bt.stream, batch_k_splits(L.gateup));
+      launch_bgemv<BG_SWIGLU>(L.gateup, a, n, d, Bt.stream);
     }
     prefill_split_kernel<false><<<n, kGemvThreads, 0, Bt.stream>>>(Bt.act.as<float>(), F, nullptr, 0.0f,
                                                                     xs, xscale);
     {
-      PrefillGemmArgs a = {};
+      BgemvArgs a = {};
+      a.xs = xs;
       a.xscale = xscale;
       a.out = H;
       a.ld_out = d;
       a.part = Bt.kpart.as<float>();
-      a.tile_cnt = Bt.tile_cnt.as<unsigned int>();
-      launch_prefill_gemm<PG_RESID, kPgBNSlots>(L.down, map_f, a, n, Bt.stream, batch_k_splits(L.down));
+      launch_bgemv<BG_RESID>(L.down, a, n, F, Bt.stream);
     }
     FABER_CUDA(cudaGetLastError());
   }

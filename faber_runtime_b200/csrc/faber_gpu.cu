@@ -368,6 +368,9 @@ void launch_gemv_rows(const GemvArgs& a, const DeviceRows& W, cudaStream_t strea
 
 struct FaberGpuQ4kTensor {
   faber::DeviceTiled t;
+  // scratch of faber_gpu_v2_q4k_gemv_batch, allocated on its first call:
+  // the x split (16 sequences x hi/lo rows), scales, slab partials
+  faber::DevBuf bxs, bscale, bpart;
 };
 
 #include "engine.cuh"
@@ -655,6 +658,34 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_gemv_exc
       throw Error(FABER_STATUS_TIMEOUT, flag == 3 ? "a grid barrier wait expired"
                                                   : "an exchange word did not carry the epoch in time");
     }
+  });
+}
+
+__attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_gemv_batch(
+    FaberGpuQ4kTensor* t, const float* x, uint32_t batch, float* y, void* stream) {
+  return guarded("faber_gpu_v2_q4k_gemv_batch", [&] {
+    FABER_ARG(t && x && y, "null pointer");
+    FABER_ARG(batch >= 1 && batch <= (uint32_t)kBgMaxSeq, "batch must be in [1, 16]");
+    require(t->t.identity, FABER_STATUS_UNSUPPORTED, "batched GEMV needs rows in whole super-blocks");
+    const cudaStream_t st = as_stream(stream);
+    const int K = t->t.cols;
+    if (!t->bxs.p) {
+      // sized for the largest batch: 16 sequences use the most slabs
+      t->bxs.alloc((size_t)2 * kBgMaxSeq * K * 2);
+      t->bscale.alloc((size_t)kBgMaxSeq * 4);
+      t->bpart.alloc(std::max<size_t>(bgemv_part_floats(t->t, kBgMaxSeq), 1) * 4);
+    }
+    __half* xs = t->bxs.as<__half>();
+    float* xscale = t->bscale.as<float>();
+    prefill_split_kernel<false><<<batch, kGemvThreads, 0, st>>>(x, K, nullptr, 0.0f, xs, xscale);
+    FABER_CUDA(cudaGetLastError());
+    BgemvArgs a = {};
+    a.xs = xs;
+    a.xscale = xscale;
+    a.out = y;
+    a.ld_out = t->t.rows;
+    a.part = t->bpart.as<float>();
+    launch_bgemv<BG_STORE>(t->t, a, (int)batch, K, st);
   });
 }
 

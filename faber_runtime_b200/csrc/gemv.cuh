@@ -5,7 +5,8 @@
 // (src/dequant.rs:194-217) after metal_f16_round_weights
 // (src/cpu_oracle.rs:356-360).
 //
-// Data path (one producer warp + 8 consumer warps per CTA, 2 CTAs per SM):
+// Data path (a producer warp, 8 consumer warps and an epilogue warp per CTA,
+// 2 CTAs per SM):
 //   * the producer streams 2304-byte tile items (16 rows x one super-block:
 //     16 headers, then 16 x 128 quant bytes) with bulk TMA copies into a
 //     3-4 stage shared-memory ring guarded by mbarriers (no multicast);
@@ -22,10 +23,10 @@
 //     mma.sync m16n8k16 (f16 x f16 -> f32) multiplies the 16x16 weight tile
 //     by [hi, lo]: accumulator columns 0 and 1 sum to y*2^-s. The tensor
 //     core is the reduction engine;
-//   * warps split K (super-blocks) and the CTA reduces the 8 partial tiles
-//     in shared memory in a fixed order (deterministic), then runs a fused
-//     epilogue (store / residual add / RoPE + KV-cache append / SwiGLU /
-//     logits + argmax).
+//   * warps split K (super-blocks); each hands its partial tile over through
+//     an mbarrier to a dedicated epilogue warp, which sums the 8 partials in
+//     a fixed order (deterministic) and runs the fused epilogue (store /
+//     residual add / RoPE + KV-cache append / SwiGLU / logits + argmax).
 #pragma once
 
 #include "common.cuh"
@@ -430,44 +431,6 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
 // ---------------------------------------------------------------------------
 // Weight item: one 16-row tile x one 256-element super-block column
 // ---------------------------------------------------------------------------
-struct Q4Regs {
-  uint4 hA, hB;        // headers of rows g and g+8
-  uint4 qA0, qA1;      // quant chunk t (32 bytes) of row g
-  uint4 qB0, qB1;      // ... of row g+8
-};
-
-template <int WL>
-__device__ __forceinline__ void q4_load(const GemvArgs& a, int tile, int b, int g, int t,
-                                        Q4Regs& r) {
-  if (WL == WL_TILED) {
-    const uint8_t* base = a.w + ((size_t)tile * a.nb + b) * kTileItemBytes;
-    r.hA = ldg_stream(base + 16 * g);
-    r.hB = ldg_stream(base + 16 * (g + 8));
-    const uint8_t* qa = base + 256 + 128 * g + 32 * t;
-    const uint8_t* qb = qa + 128 * 8;
-    r.qA0 = ldg_stream(qa);
-    r.qA1 = ldg_stream(qa + 16);
-    r.qB0 = ldg_stream(qb);
-    r.qB1 = ldg_stream(qb + 16);
-  } else {
-    const int ra = tile * kTileRows + g, rb = ra + 8;
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    r.hA = r.hB = r.qA0 = r.qA1 = r.qB0 = r.qB1 = z;
-    if (ra < a.n_rows) {
-      const uint8_t* p = a.w + ((size_t)ra * a.nb + b) * kQ4kBlockBytes;
-      r.hA = ldg_stream(p);
-      r.qA0 = ldg_stream(p + 16 + 32 * t);
-      r.qA1 = ldg_stream(p + 32 + 32 * t);
-    }
-    if (rb < a.n_rows) {
-      const uint8_t* p = a.w + ((size_t)rb * a.nb + b) * kQ4kBlockBytes;
-      r.hB = ldg_stream(p);
-      r.qB0 = ldg_stream(p + 16 + 32 * t);
-      r.qB1 = ldg_stream(p + 32 + 32 * t);
-    }
-  }
-}
-
 // One-instruction (w & MASK) | magic, with the magic in a register operand.
 template <uint32_t MASK>
 __device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t magic) {
@@ -576,58 +539,181 @@ __device__ __forceinline__ RowScales3 row_scales3(const uint4 h, int t, const La
   return r;
 }
 
-__device__ __forceinline__ void dequant_word3(uint32_t w, const RowScales3& s, const LaneConst& lc,
-                                              uint32_t& lo0, uint32_t& lo2, uint32_t& hi0,
-                                              uint32_t& hi2) {
-  const uint32_t u = w >> 8;
-  const uint32_t l02 = hfma2_u(and_or<0x000f000fu>(w, lc.m1024), s.sclo2, s.clo2);
-  const uint32_t l13 = hfma2_u(and_or<0x000f000fu>(u, lc.m1024), s.sclo2, s.clo2);
-  const uint32_t h02 = hfma2_u(and_or<0x00f000f0u>(w, lc.m64), s.schi2, s.chi2);
-  const uint32_t h13 = hfma2_u(and_or<0x00f000f0u>(u, lc.m64), s.schi2, s.chi2);
-  const float2 a = mixed_fma_pair(l02, s.dword, s.nm1);
-  const float2 b = mixed_fma_pair(l13, s.dword, s.nm1);
-  const float2 c = mixed_fma_pair(h02, s.dword, s.nm2);
-  const float2 d = mixed_fma_pair(h13, s.dword, s.nm2);
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMV item: lane (g, t) of a consumer warp forms rows g and g+8 of
+// its 32-byte quant chunk t (sub-blocks 2t, 2t+1) of one 16-row item.
+// Instruction budget per 8 weights (one quant word): 4 mask-or (ALU), one
+// high multiply for the byte shift (FMA pipe, so the ALU pipe, which issues
+// at half rate, only carries the mask-or and the f16 pack), 4 f16x2 FMAs,
+// 8 mixed FMAs and 4 packs.
+// ---------------------------------------------------------------------------
+struct ItemConst {
+  uint32_t m1024;     // 0x64006400
+  uint32_t m64;       // 0x54005400
+  uint32_t sh24;      // 2^24: (w >> 8) as mul.hi (kept opaque in a register)
+  uint32_t sel;       // byte selector of this lane's scale / min source bytes
+  uint32_t mlo, mhi;  // masks of the 6- or 4-bit low part and the 2-bit high part
+  uint32_t msh;       // right shift of the min's low part (0 or 4)
+};
+
+__device__ __forceinline__ ItemConst item_const(int t) {
+  ItemConst c;
+  asm("mov.b32 %0, 0x64006400;" : "=r"(c.m1024));
+  asm("mov.b32 %0, 0x54005400;" : "=r"(c.m64));
+  asm("mov.b32 %0, 0x01000000;" : "=r"(c.sh24));
+  const uint32_t k = 2u * (uint32_t)(t & 1);
+  if (t < 2) {
+    c.sel = k | ((k + 1u) << 4) | (k << 8) | ((k + 1u) << 12);
+    c.mlo = 0x3f3fu;
+    c.mhi = 0u;
+    c.msh = 0u;
+  } else {
+    c.sel = (4u + k) | ((5u + k) << 4) | (k << 8) | ((k + 1u) << 12);
+    c.mlo = 0x0f0fu;
+    c.mhi = 0x3030u;
+    c.msh = 4u;
+  }
+  return c;
+}
+
+// Per (row, lane): the formation constants of sub-blocks a = 2t and b = 2t+1.
+struct RowScales {
+  uint32_t scp;     // (sc_a, sc_b) f16x2
+  uint32_t ca, cb;  // (-1024 sc_a) x2 and (-64 sc_b) x2: the magic offsets
+  float nma, nmb;   // -(dmin * m_a), -(dmin * m_b)
+  uint32_t dword;   // header word 0: d in the low half, dmin in the high half
+};
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t m, uint32_t c) {
+  uint32_t d;  // (a & m) | c
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t mulhi_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// (lo(b), lo(b)) * c and (hi(b), hi(b)) * c, the broadcast as an operand swizzle.
+__device__ __forceinline__ uint32_t hmul2_lo(uint32_t bpair, uint32_t c) {
+  uint32_t d;
+  asm("{\n .reg .b16 l, h;\n .reg .b32 bb;\n mov.b32 {l, h}, %1;\n mov.b32 bb, {l, l};\n"
+      " mul.rn.f16x2 %0, bb, %2;\n}"
+      : "=r"(d) : "r"(bpair), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2_hi(uint32_t bpair, uint32_t c) {
+  uint32_t d;
+  asm("{\n .reg .b16 l, h;\n .reg .b32 bb;\n mov.b32 {l, h}, %1;\n mov.b32 bb, {h, h};\n"
+      " mul.rn.f16x2 %0, bb, %2;\n}"
+      : "=r"(d) : "r"(bpair), "r"(c));
+  return d;
+}
+// a * (lo(b), lo(b)) + c and a * (hi(b), hi(b)) + c
+__device__ __forceinline__ uint32_t hfma2_lo(uint32_t a, uint32_t bpair, uint32_t c) {
+  uint32_t d;
+  asm("{\n .reg .b16 l, h;\n .reg .b32 bb;\n mov.b32 {l, h}, %2;\n mov.b32 bb, {l, l};\n"
+      " fma.rn.f16x2 %0, %1, bb, %3;\n}"
+      : "=r"(d) : "r"(a), "r"(bpair), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_hi(uint32_t a, uint32_t bpair, uint32_t c) {
+  uint32_t d;
+  asm("{\n .reg .b16 l, h;\n .reg .b32 bb;\n mov.b32 {l, h}, %2;\n mov.b32 bb, {h, h};\n"
+      " fma.rn.f16x2 %0, %1, bb, %3;\n}"
+      : "=r"(d) : "r"(a), "r"(bpair), "r"(c));
+  return d;
+}
+
+// get_scale_min_k4 (src/dequant.rs:178-187) for this lane's two sub-blocks,
+// branch-free. Bytes s[0..11] are header words y, z, w:
+//   t < 2  (j = 2t, 2t+1):   sc = s[j] & 63,                     m = s[j+4] & 63
+//   t >= 2 (j = 2t, 2t+1):   sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4,
+//                            m  = (s[j+4] >> 4) | (s[j] >> 6) << 4
+// One byte permute gathers [low-part bytes, high-part bytes] per field.
+__device__ __forceinline__ RowScales row_scales(const uint4 h, const ItemConst& ic) {
+  const uint32_t X = prmt_r(h.y, h.w, ic.sel);
+  const uint32_t Y = prmt_r(h.z, h.w, ic.sel);
+  const uint32_t sc16 = lop3_and_or(X, ic.mlo, (X >> 18) & ic.mhi);
+  const uint32_t m16 = lop3_and_or(Y >> ic.msh, ic.mlo, (Y >> 18) & ic.mhi);
+  // (1024 + v_a, 1024 + v_b) as f16x2, minus 1024: exact small integers
+  const uint32_t k1024 = ic.m1024;
+  const uint32_t scp = hsub2_u(prmt<0x7150>(sc16, k1024), k1024);
+  const uint32_t mp = hsub2_u(prmt<0x7150>(m16, k1024), k1024);
+  RowScales r;
+  r.scp = scp;
+  r.ca = hmul2_lo(scp, 0xe400e400u);  // * -1024
+  r.cb = hmul2_hi(scp, 0xd400d400u);  // * -64
+  // m1 = dmin * m exactly; its negation keeps the reference's d1*q - m1
+  // (sign of zero included)
+  const float2 m12 = mixed_mul_hi_pair(mp, h.x);
+  r.nma = -m12.x;
+  r.nmb = -m12.y;
+  r.dword = h.x;
+  return r;
+}
+
+// Eight exact f16-rounded weights of one quant word: pairs (e, e+2) and
+// (e+1, e+3) of sub-block a (low nibbles) and of sub-block b (high nibbles).
+__device__ __forceinline__ void dequant_word(uint32_t w, const RowScales& s, const ItemConst& ic,
+                                             uint32_t& lo0, uint32_t& lo2, uint32_t& hi0,
+                                             uint32_t& hi2) {
+  const uint32_t u = mulhi_u(w, ic.sh24);  // w >> 8
+  const uint32_t l02 = hfma2_lo(and_or<0x000f000fu>(w, ic.m1024), s.scp, s.ca);
+  const uint32_t l13 = hfma2_lo(and_or<0x000f000fu>(u, ic.m1024), s.scp, s.ca);
+  const uint32_t h02 = hfma2_hi(and_or<0x00f000f0u>(w, ic.m64), s.scp, s.cb);
+  const uint32_t h13 = hfma2_hi(and_or<0x00f000f0u>(u, ic.m64), s.scp, s.cb);
+  const float2 a = mixed_fma_pair(l02, s.dword, s.nma);
+  const float2 b = mixed_fma_pair(l13, s.dword, s.nma);
+  const float2 c = mixed_fma_pair(h02, s.dword, s.nmb);
+  const float2 d = mixed_fma_pair(h13, s.dword, s.nmb);
   lo0 = pack_half2(a.x, a.y);  // (e, e+2)
   lo2 = pack_half2(b.x, b.y);  // (e+1, e+3)
   hi0 = pack_half2(c.x, c.y);
   hi2 = pack_half2(d.x, d.y);
 }
 
-__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
-  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
-}
+// Byte offsets inside one staged item (shared memory): tiled = 16 headers
+// then 16 x 128 quant bytes; native = 16 consecutive 144-byte blocks.
+template <int WL>
+struct ItemGeom {
+  static constexpr int kHead = WL == WL_TILED ? 16 : kQ4kBlockBytes;       // header of row g
+  static constexpr int kQuant0 = WL == WL_TILED ? 256 : 16;                // quants of row 0
+  static constexpr int kQuantRow = WL == WL_TILED ? 128 : kQ4kBlockBytes;  // quant row stride
+};
 
-// 16 MMAs of one Q4_K item into four independent accumulator chains (MMA m
-// goes to chain m & 3, so consecutive MMAs do not wait on each other).
-// B fragments come from lane groups 0 (hi column) and 1 (lo column); the
-// other groups load the same rows (a free shared-memory broadcast, no
-// predication) and their values only reach accumulator columns 2..7, which
-// are never read.
-__device__ __forceinline__ void q4_compute(const Q4Regs& r, int t, const __half* xsrc, int xbase,
-                                           float (&acc)[4][4], const LaneConst& lc) {
-  const RowScales3 sA = row_scales3(r.hA, t, lc);
-  const RowScales3 sB = row_scales3(r.hB, t, lc);
+// One item: 16 MMAs into four independent accumulator chains (MMA m goes to
+// chain m & 3). B fragments come from lane groups 0 (x hi) and 1 (x lo); the
+// other groups load the same rows (a shared-memory broadcast) and feed
+// accumulator columns 2..7, which are never read. xlo / xhi point at the
+// padded x elements 64t + {0..15} and 64t + 32 + {0..15} of the item.
+template <int WL>
+__device__ __forceinline__ void q4_item(const uint8_t* hdr, const uint8_t* qnt, const __half* xlo,
+                                        const __half* xhi, float (&acc)[4][4], const ItemConst& ic) {
+  using G = ItemGeom<WL>;
+  const uint4 hA = *reinterpret_cast<const uint4*>(hdr);
+  const uint4 hB = *reinterpret_cast<const uint4*>(hdr + 8 * G::kHead);
+  const RowScales sA = row_scales(hA, ic);
+  const RowScales sB = row_scales(hB, ic);
 #pragma unroll
   for (int pp = 0; pp < 2; ++pp) {
-    const uint4 qa = pp ? r.qA1 : r.qA0;
-    const uint4 qb = pp ? r.qB1 : r.qB0;
-    // B fragments: elements e = 64t + 32n + 16pp + 4i of this super-block;
-    // v0 is a multiple of 16, so +8 stays inside its 64-group.
-    uint4 xb_lo0, xb_lo1, xb_hi0, xb_hi1;
-    {
-      const int v0 = xbase + 64 * t + 16 * pp;
-      const int p0 = xs_index(v0), p1 = xs_index(v0 + 32);
-      xb_lo0 = *reinterpret_cast<const uint4*>(xsrc + p0);
-      xb_lo1 = *reinterpret_cast<const uint4*>(xsrc + p0 + 8);
-      xb_hi0 = *reinterpret_cast<const uint4*>(xsrc + p1);
-      xb_hi1 = *reinterpret_cast<const uint4*>(xsrc + p1 + 8);
-    }
+    const uint4 qa = *reinterpret_cast<const uint4*>(qnt + 16 * pp);
+    const uint4 qb = *reinterpret_cast<const uint4*>(qnt + 16 * pp + 8 * G::kQuantRow);
+    const uint4 xb_lo0 = *reinterpret_cast<const uint4*>(xlo + 16 * pp);
+    const uint4 xb_lo1 = *reinterpret_cast<const uint4*>(xlo + 16 * pp + 8);
+    const uint4 xb_hi0 = *reinterpret_cast<const uint4*>(xhi + 16 * pp);
+    const uint4 xb_hi1 = *reinterpret_cast<const uint4*>(xhi + 16 * pp + 8);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t aL0, aL2, aH0, aH2, bL0, bL2, bH0, bH2;
-      dequant_word3(word_of(qa, i), sA, lc, aL0, aL2, aH0, aH2);
-      dequant_word3(word_of(qb, i), sB, lc, bL0, bL2, bH0, bH2);
+      dequant_word(word_of(qa, i), sA, ic, aL0, aL2, aH0, aH2);
+      dequant_word(word_of(qb, i), sB, ic, bL0, bL2, bH0, bH2);
       const uint4& xl = (i < 2) ? xb_lo0 : xb_lo1;
       const uint4& xh = (i < 2) ? xb_hi0 : xb_hi1;
       const uint32_t xl0 = (i & 1) ? xl.z : xl.x, xl1 = (i & 1) ? xl.w : xl.y;
@@ -637,32 +723,6 @@ __device__ __forceinline__ void q4_compute(const Q4Regs& r, int t, const __half*
       mma_16816(cl[0], cl[1], cl[2], cl[3], aL0, bL0, aL2, bL2, xl0, xl1);
       mma_16816(ch[0], ch[1], ch[2], ch[3], aH0, bH0, aH2, bH2, xh0, xh1);
     }
-  }
-}
-
-// Load one item's registers from the shared-memory ring (the byte layout of
-// the global item: tiled = 16 headers then 16 x 128 quant bytes; native = 16
-// consecutive 144-byte blocks).
-template <int WL>
-__device__ __forceinline__ void q4_lds(const uint8_t* item, int g, int t, Q4Regs& r) {
-  if (WL == WL_TILED) {
-    r.hA = *reinterpret_cast<const uint4*>(item + 16 * g);
-    r.hB = *reinterpret_cast<const uint4*>(item + 16 * (g + 8));
-    const uint8_t* qa = item + 256 + 128 * g + 32 * t;
-    const uint8_t* qb = qa + 128 * 8;
-    r.qA0 = *reinterpret_cast<const uint4*>(qa);
-    r.qA1 = *reinterpret_cast<const uint4*>(qa + 16);
-    r.qB0 = *reinterpret_cast<const uint4*>(qb);
-    r.qB1 = *reinterpret_cast<const uint4*>(qb + 16);
-  } else {
-    const uint8_t* ra = item + kQ4kBlockBytes * g;
-    const uint8_t* rb = item + kQ4kBlockBytes * (g + 8);
-    r.hA = *reinterpret_cast<const uint4*>(ra);
-    r.qA0 = *reinterpret_cast<const uint4*>(ra + 16 + 32 * t);
-    r.qA1 = *reinterpret_cast<const uint4*>(ra + 32 + 32 * t);
-    r.hB = *reinterpret_cast<const uint4*>(rb);
-    r.qB0 = *reinterpret_cast<const uint4*>(rb + 16 + 32 * t);
-    r.qB1 = *reinterpret_cast<const uint4*>(rb + 32 + 32 * t);
   }
 }
 
@@ -880,12 +940,15 @@ inline size_t gemv_smem_bytes(int nb) {
 // ---------------------------------------------------------------------------
 // Pipelined Q4_K kernel: one producer warp streams tile items with bulk TMA
 // copies (cp.async.bulk, no multicast) into a shared-memory ring guarded by
-// mbarriers; 8 consumer warps dequantize from shared memory. One CTA per SM,
-// persistent over tiles, so that under programmatic dependent launch the
-// next kernel's producer can already stream its weights.
+// mbarriers; 8 consumer warps dequantize from shared memory. Two CTAs per SM
+// (one where the staged x needs more than half the shared memory),
+// persistent over tiles; under programmatic dependent launch the producer
+// starts streaming before the previous kernel has finished.
 // ---------------------------------------------------------------------------
 constexpr int kConsumerWarps = kGemvWarps;
-constexpr int kPipeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kProducerWarp = kConsumerWarps;      // streams the ring
+constexpr int kEpilogueWarp = kConsumerWarps + 1;  // sums partial tiles, runs the epilogue
+constexpr int kPipeThreads = (kConsumerWarps + 2) * 32;
 constexpr int kStageBytes = kConsumerWarps * kTileItemBytes;  // 18 KB
 constexpr int kMaxStages = 4;
 constexpr uint32_t kSpinLimit = 1u << 20;
@@ -938,6 +1001,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Partial tiles in flight between the consumer warps and the epilogue warp:
+// each consumer hands its 16 partial rows of a tile over through an
+// mbarrier and goes on; a dedicated epilogue warp sums them and runs the
+// epilogue, so neither a barrier nor the epilogue's memory round trips sit
+// between a consumer's tiles (it waits only when kParts tiles ahead).
+constexpr int kParts = 4;
+
 struct PipeLayout {
   int stages;
   size_t ring, xs, part, redd, redf, bars, total;
@@ -949,10 +1019,10 @@ __host__ __device__ inline PipeLayout pipe_layout(int nb) {
   L.ring = 0;
   L.xs = (size_t)L.stages * kStageBytes;
   L.part = L.xs + (size_t)2 * gemv_xs_halves(nb) * 2;
-  L.redd = L.part + (size_t)2 * kConsumerWarps * kTileRows * 4;
+  L.redd = L.part + (size_t)kParts * kConsumerWarps * kTileRows * 4;
   L.redf = L.redd + (size_t)kConsumerWarps * 8;
-  L.bars = (L.redf + (size_t)kConsumerWarps * 4 + 7) & ~(size_t)7;
-  L.total = L.bars + (size_t)2 * kMaxStages * 8;
+  L.bars = (L.redf + (size_t)kConsumerWarps * 4 + 8 + 7) & ~(size_t)7;  // + out_scale
+  L.total = L.bars + (size_t)(2 * kMaxStages + 2 * kParts) * 8;
   return L;
 }
 
@@ -970,6 +1040,8 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
   float* redf = reinterpret_cast<float*>(smem + L.redf);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + kMaxStages;
+  uint64_t* pfull = empty + kMaxStages;  // a tile's partials written by all consumer warps
+  uint64_t* pfree = pfull + kParts;      // ... and summed by its epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = L.stages;
@@ -979,11 +1051,15 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    for (int p = 0; p < kParts; ++p) {
+      mbar_init(&pfull[p], kConsumerWarps);
+      mbar_init(&pfree[p], 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kProducerWarp) {
     // producer: weights never depend on the previous kernel, so no wait here
     if (lane == 0) {
       uint64_t policy;
@@ -997,11 +1073,10 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
           const int cnt = min(kConsumerWarps, a.nb - b0);
           uint8_t* dst = ring + (size_t)s * kStageBytes;
           if (WL == WL_TILED) {
+            // the cnt items of one tile round are contiguous: one copy
             mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * kTileItemBytes));
-            for (int w = 0; w < cnt; ++w)
-              bulk_g2s(dst + w * kTileItemBytes,
-                       a.w + ((size_t)tile * a.nb + b0 + w) * kTileItemBytes, kTileItemBytes,
-                       &full[s], policy);
+            bulk_g2s(dst, a.w + ((size_t)tile * a.nb + b0) * kTileItemBytes,
+                     (uint32_t)(cnt * kTileItemBytes), &full[s], policy);
           } else {
             const int rows = min(kTileRows, a.n_rows - tile * kTileRows);
             mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * rows * kQ4kBlockBytes));
@@ -1021,34 +1096,66 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
     return;
   }
 
+  if (warp == kEpilogueWarp) {
+    // epilogue: tile by tile in order, the 8 partial tiles summed in warp
+    // order (deterministic), then the fused epilogue on lanes 0-7
+    pdl_wait();
+    float out_scale = 0.f;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++it) {
+      const int pi = it % kParts;
+      mbar_wait(&pfull[pi], (uint32_t)((it / kParts) & 1));
+      if (it == 0) out_scale = *reinterpret_cast<volatile float*>(redf + kConsumerWarps);
+      const float* pb = part + pi * kConsumerWarps * kTileRows;
+      if (lane < 8) {
+        const int p = lane;
+        float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          y0 += pb[w * kTileRows + 2 * p];
+          y1 += pb[w * kTileRows + 2 * p + 1];
+        }
+        gemv_epilogue<EPI>(a, tile, p, y0 * out_scale, y1 * out_scale);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfree[pi]);
+    }
+    return;
+  }
+
   // consumers
   pdl_wait();
   const float out_scale = stage_x<PRO, true, true>(a, xh, xl, redd, redf);
   pdl_launch_dependents();
+  // for the epilogue warp (read after the first tile's hand-over)
+  if (threadIdx.x == 0) redf[kConsumerWarps] = out_scale;
   const int g = lane >> 2, t = lane & 3;
+  const ItemConst ic = item_const(t);
   const __half* xsrc = (g == 0) ? xh : xl;
-  LaneConst lc;  // magics kept in registers (one lop3 per mask-or)
-  {
-    const uint32_t k = 2u * (uint32_t)(t & 1);
-    lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
-    asm("mov.b32 %0, 0x64006400;" : "=r"(lc.m1024));
-    asm("mov.b32 %0, 0x54005400;" : "=r"(lc.m64));
-  }
-  const uint8_t* my_item = ring + warp * kTileItemBytes;
+  using G = ItemGeom<WL>;
+  // this warp's item inside a slot: header of row g, quant chunk t of row g
+  const int off_h = warp * kTileItemBytes + G::kHead * g;
+  const int off_q = warp * kTileItemBytes + G::kQuant0 + G::kQuantRow * g + 32 * t;
+  // consecutive rounds of a warp are 8 super-blocks (2048 elements) apart:
+  // 2304 padded halves
+  constexpr int kRoundHalves = kConsumerWarps * 256 + ((kConsumerWarps * 256) >> 3);
   int s = 0, it = 0;
   uint32_t ph = 0;
   for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++it) {
     float acc[4][4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+    // x elements of this warp's first item: xb0 + {0..15, 32..47} (+16pp);
+    // xoff is a multiple of 32, so neither run of 32 crosses a padding gap
     const int xoff = a.tile_xoff ? a.tile_xoff[tile] : 0;
-    int xbase = kXPad + warp * 256 - xoff;
-    for (int b = warp; b < R * kConsumerWarps; b += kConsumerWarps, xbase += kConsumerWarps * 256) {
+    const int xb0 = kXPad + warp * 256 - xoff + 64 * t;
+    const __half* xlo = xsrc + xs_index(xb0);
+    const __half* xhi = xsrc + xs_index(xb0 + 32);
+    for (int r = 0, b = warp; r < R; ++r, b += kConsumerWarps) {
       mbar_wait(&full[s], ph);
       if (b < a.nb) {
-        Q4Regs reg;
-        q4_lds<WL>(my_item + (size_t)s * kStageBytes, g, t, reg);
-        q4_compute(reg, t, xsrc, xbase, acc, lc);
+        const uint8_t* slot = ring + (size_t)s * kStageBytes;
+        q4_item<WL>(slot + off_h, slot + off_q, xlo, xhi, acc, ic);
       }
       // release the slot once every lane has consumed its bytes
       __syncwarp();
@@ -1057,8 +1164,13 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
         s = 0;
         ph ^= 1u;
       }
+      xlo += kRoundHalves;
+      xhi += kRoundHalves;
     }
-    float* pb = part + (it & 1) * kConsumerWarps * kTileRows;
+    // hand this warp's partial rows to the epilogue warp
+    const int pi = it % kParts;
+    float* pb = part + pi * kConsumerWarps * kTileRows;
+    if (it >= kParts) mbar_wait(&pfree[pi], (uint32_t)(((it / kParts) & 1) ^ 1));
     if (t == 0) {
       const float a0 = (acc[0][0] + acc[0][1]) + (acc[1][0] + acc[1][1]) +
                        (acc[2][0] + acc[2][1]) + (acc[3][0] + acc[3][1]);
@@ -1067,17 +1179,8 @@ __global__ void __launch_bounds__(kPipeThreads, 2) gemv_pipe_kernel(const GemvAr
       pb[warp * kTileRows + g] = a0;
       pb[warp * kTileRows + g + 8] = a1;
     }
-    cbar<true>();
-    if (threadIdx.x < 8) {
-      const int p = threadIdx.x;
-      float y0 = 0.f, y1 = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        y0 += pb[w * kTileRows + 2 * p];
-        y1 += pb[w * kTileRows + 2 * p + 1];
-      }
-      gemv_epilogue<EPI>(a, tile, p, y0 * out_scale, y1 * out_scale);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&pfull[pi]);
   }
 }
 

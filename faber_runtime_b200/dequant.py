@@ -54,6 +54,12 @@ class Q4kTensor:
     def gemv(self, x_ptr: int, y_ptr: int, stream: int = 0) -> None:
         _lib.call("faber_gpu_v2_q4k_gemv", self._h, x_ptr, y_ptr, stream)
 
+    def gemv_batch(self, x_ptr: int, batch: int, y_ptr: int, stream: int = 0) -> None:
+        """y[b] = dense(w, x[b]) for b < batch (1..16): x [batch][cols] and y
+        [batch][rows] f32 device arrays; each exact weight fragment serves
+        every sequence."""
+        _lib.call("faber_gpu_v2_q4k_gemv_batch", self._h, x_ptr, int(batch), y_ptr, stream)
+
     def dequant_rows(self, out_ptr: int, f16_round: bool = True, stream: int = 0) -> None:
         _lib.call("faber_gpu_v2_q4k_dequant_rows", self._h, out_ptr, int(f16_round), stream)
 

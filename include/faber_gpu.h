@@ -177,6 +177,15 @@ FaberRtStatusV1 faber_gpu_v2_q4k_gemv_exchange(const FaberGpuQ4kTensor* t, const
                                                const float* norm_w, float eps, const uint64_t* exchange,
                                                uint32_t tp, uint32_t epoch, uint32_t wait_limit,
                                                float* x_sum_out, float* y, void* stream);
+/* Batched dense over the resident weight, the per-sequence linear of a
+ * batched decode step (src/decoder_ops.rs:378-406 for each of `batch`
+ * inputs): y[b] = dense(w, x[b]) for b < batch <= 16, x [batch][cols] and
+ * y [batch][rows] f32 device arrays. Every exact weight fragment is formed
+ * once for all sequences. Rows must be in whole super-blocks. The tensor
+ * keeps its scratch after the first call; calls on one tensor must not
+ * overlap. */
+FaberRtStatusV1 faber_gpu_v2_q4k_gemv_batch(FaberGpuQ4kTensor* t, const float* x, uint32_t batch,
+                                            float* y, void* stream);
 /* Dequantize the resident (repacked) weight back to [rows][cols] f32 —
  * proves the repack is value-identical to dequant_tensor. */
 FaberRtStatusV1 faber_gpu_v2_q4k_dequant_rows(const FaberGpuQ4kTensor* t, float* out,

@@ -2,7 +2,10 @@
 
 Several sessions of one model, each with its own prompt (short ones pushed
 token by token, long ones through the tensor-core prompt pass), decode in
-lockstep: every linear layer is one tcgen05 Q4_K GEMM over all sequences.
+lockstep: every linear layer is one batched Q4_K GEMV over all sequences
+(each exact weight fragment feeds 1, 2 or 4 MMA column blocks for up to 4, 8
+or 16 sequences; the 2816-wide down projection at 16 sequences is cut into
+two K slabs summed through the per-tile ticket).
 Each sequence's tokens must equal the oracle's run_greedy for its prompt
 alone, and afterwards each session must hold its own state: its
 position_logits equal the oracle's logits that chose its last token
@@ -44,6 +47,8 @@ def pair(cuda):
 
 @pytest.mark.parametrize("lengths", [
     [40, 7, 100, 33, 64],                # mixed: token-by-token and prompt-pass prompts
+    [20, 45, 70],                        # one MMA column block
+    [9 * i + 5 for i in range(8)],       # two full column blocks
     [33 + i for i in range(16)],         # a full batch of 16
 ])
 def test_batch_greedy_matches_oracle(pair, lengths):

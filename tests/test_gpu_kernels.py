@@ -141,6 +141,32 @@ def test_gemv_q4k_matches_oracle(cuda, oracle, rows, cols):
         within(y2.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("rows,cols,batch", [
+    (4096, 4096, 1),
+    (4096, 4096, 3),      # one MMA column block, padding columns
+    (100, 1024, 8),       # partial last tile, two column blocks
+    (4096, 11008, 16),    # four column blocks, six K slabs summed in order
+    (2816, 2048, 13),
+])
+def test_batched_gemv_matches_oracle(cuda, oracle, rows, cols, batch):
+    """faber_gpu_v2_q4k_gemv_batch: each sequence's output equals the
+    oracle's dense of that sequence's input (the batched decode's linear)."""
+    from faber_runtime_b200 import dequant, synth
+    blocks = synth.q4k_blocks(23, rows + 7 * cols, rows * cols // 256)
+    xs = np.stack([synth.normal(23, 100 + b, cols) * np.float32(1.0 + b) for b in range(batch)])
+    t = dequant.Q4kTensor(blocks, rows, cols)
+    dx = to_dev(xs)
+    y = torch.full((batch, rows), float("nan"), dtype=torch.float32, device=cuda)
+    for _ in range(2):  # the second call reuses the tensor's scratch
+        t.gemv_batch(dx.data_ptr(), batch, y.data_ptr())
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        for b in range(batch):
+            ref = oracle.dense_q(oracle.Q4_K, blocks, xs[b], cols, rows, f16_round=True)
+            assert within(got[b], ref) < 1e-4
+    t.close()
+
+
 @pytest.mark.parametrize("scale", [0.0, 1e-30, 1e-6, 1e8, 3e30])
 def test_gemv_dynamic_range(cuda, oracle, scale):
     from faber_runtime_b200 import dequant, synth
