@@ -1169,7 +1169,7 @@ inline CUtensorMap xs_tensor_map(const __half* xs, uint64_t rows, uint64_t K, in
 
 template <int EPI, int BN = kPgBN>
 void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGemmArgs a, int n_tok,
-                         cudaStream_t stream, int k_splits = 1) {
+                         cudaStream_t stream) {
   auto kern = prefill_gemm_kernel<EPI, BN>;
   constexpr int kPgSmemBytes = PgLayout<BN>::kBytes;
   static thread_local std::map<int, bool> attr_done;
@@ -1185,12 +1185,7 @@ void launch_prefill_gemm(const DeviceTiled& W, const CUtensorMap& map, PrefillGe
   a.nb = W.nb;
   a.m_rows = W.rows;
   a.n_tok = n_tok;
-  if (k_splits > 1) {
-    a.k_chunk = (W.nb + k_splits - 1) / k_splits;
-    k_splits = (W.nb + a.k_chunk - 1) / a.k_chunk;  // no empty split
-    require(a.part != nullptr && a.tile_cnt != nullptr, FABER_STATUS_UNSUPPORTED, "split K without scratch");
-  }
-  const dim3 grid((2 * n_tok + BN - 1) / BN, (W.rows + kPgBM - 1) / kPgBM, std::max(1, k_splits));
+  const dim3 grid((2 * n_tok + BN - 1) / BN, (W.rows + kPgBM - 1) / kPgBM);
   kern<<<grid, kPgThreads, kPgSmemBytes, stream>>>(map, a);
   FABER_CUDA(cudaGetLastError());
 }
@@ -1484,7 +1479,7 @@ inline int64_t run_step_greedy(SessionState& S, int64_t token, const int64_t* eo
 // The sessions keep their state: afterwards each holds its sequence's
 // residual, length and cache, and its own calls continue from there.
 // ---------------------------------------------------------------------------
-constexpr int kBatchMax = kPgBNSlots / 2;
+constexpr int kBatchMax = kBgMaxSeq;
 
 struct BatchState {
   std::vector<SessionState*> seq;
@@ -1492,7 +1487,7 @@ struct BatchState {
   cudaStream_t stream = nullptr;
   DevBuf slots;  // SlotRef [L][B]
   DevBuf h, xs, xscale, q, ctx, act, logits, attn_part, attn_counters, gen;
-  DevBuf kpart, tile_cnt;  // split-K partial tiles and per-tile tickets
+  DevBuf kpart;  // the batched GEMV's slab partials
   cudaGraphExec_t g_step = nullptr, g_logits = nullptr;
   std::vector<int64_t> graph_eog;
   bool graphs_valid = false;
@@ -1511,18 +1506,6 @@ struct BatchState {
     if (cur >= 0) cudaSetDevice(cur);
   }
 };
-
-// K splits for a batched-decode GEMM: as many as keep the grid within one
-// wave (one CTA per SM) when the weight has fewer 128-row tiles than SMs (at
-// most 8 splits, whole super-blocks).
-inline int batch_k_splits(const DeviceTiled& W) {
-  const int m_tiles = (W.rows + kPgBM - 1) / kPgBM;
-  const int sms = device_info().sms;
-  if (2 * m_tiles > sms) return 1;
-  const int want = std::min(std::min(8, W.nb), sms / m_tiles);
-  const int chunk = (W.nb + want - 1) / want;
-  return (W.nb + chunk - 1) / chunk;
-}
 
 inline bool batch_supported(const ModelState& M) {
   return prefill_supported(M) && !M.cfg.tied_head && M.head.identity;
@@ -1615,8 +1598,8 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   FABER_CUDA(cudaMemcpy(Bt.slots.p, refs.data(), Bt.slots.n, cudaMemcpyHostToDevice));
   const size_t kmax = std::max((size_t)d, std::max((size_t)nq, (size_t)M.Fl));
   Bt.h.alloc((size_t)n * d * 4);
-  // the activation tile always spans kPgBNSlots rows; rows past 2n stay zero
-  Bt.xs.alloc((size_t)kPgBNSlots * kmax * 2);
+  // the hi/lo split of every sequence's input row (2n rows of the widest K)
+  Bt.xs.alloc((size_t)2 * n * kmax * 2);
   FABER_CUDA(cudaMemset(Bt.xs.p, 0, Bt.xs.n));
   Bt.xscale.alloc((size_t)kBatchMax * 4);
   FABER_CUDA(cudaMemset(Bt.xscale.p, 0, Bt.xscale.n));
@@ -1630,13 +1613,9 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   FABER_CUDA(cudaMemset(Bt.attn_counters.p, 0, Bt.attn_counters.n));
   Bt.gen_cap = Bt.max_ctx;
   Bt.gen.alloc((size_t)n * Bt.gen_cap * 8, kLedgerConcurrent);
-  size_t part = 0, tiles = 0;
-  auto need = [&](const DeviceTiled& W) {
-    const size_t m_tiles = (W.rows + kPgBM - 1) / kPgBM;
-    const int sp = batch_k_splits(W);
-    if (sp > 1) part = std::max(part, m_tiles * sp * kPgBM * kPgBNSlots);
-    tiles = std::max(tiles, m_tiles);
-  };
+  // the batched GEMV's slab partials (the largest over the step's linears)
+  size_t part = 0;
+  auto need = [&](const DeviceTiled& W) { part = std::max(part, bgemv_part_floats(W, n)); };
   for (const LayerDev& L : M.layers) {
     need(L.qkv);
     need(L.o);
@@ -1644,25 +1623,7 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
     need(L.down);
   }
   need(M.head);
-  // the batched GEMV's slab partials and tickets
-  size_t bpart = 0, btiles = 0;
-  auto bneed = [&](const DeviceTiled& W) {
-    bpart = std::max(bpart, bgemv_part_floats(W, n));
-    btiles = std::max(btiles, (size_t)W.n_tiles);
-  };
-  for (const LayerDev& L : M.layers) {
-    bneed(L.qkv);
-    bneed(L.o);
-    bneed(L.gateup);
-    bneed(L.down);
-  }
-  bneed(M.head);
-  part = std::max(part, bpart);
-  tiles = std::max(tiles, btiles);
   Bt.kpart.alloc(std::max<size_t>(part, 1) * 4);
-  Bt.tile_cnt.alloc(tiles * 4);
-  FABER_CUDA(cudaMemset(Bt.tile_cnt.p, 0, Bt.tile_cnt.n));
-  (void)tmap_encoder();  // resolved before any graph capture
 }
 
 // The head over the batch's residual rows: logits, argmax keys, next tokens.

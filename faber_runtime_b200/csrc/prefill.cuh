@@ -39,7 +39,6 @@ namespace faber {
 
 constexpr int kPgBM = 128;
 constexpr int kPgBN = 256;       // activation columns per tile in the prompt pass (128 tokens)
-constexpr int kPgBNSlots = 32;   // ... in batched decode (up to 16 sequences)
 constexpr int kPgBK = 64;
 constexpr int kPgAStages = 6;    // dequantized weight tiles in flight
 constexpr int kPgBStages = 4;    // activation tiles in flight
@@ -68,9 +67,7 @@ enum PrefillEpi : int {
   PG_STORE = 0,   // out[t][m] = y
   PG_RESID = 1,   // out[t][m] += y (residual_add, src/decoder_ops.rs:420-427)
   PG_SWIGLU = 2,  // rows interleaved gate/up: out[t][m/2] = silu(g) * u
-  PG_QKV = 3,     // RoPE on Q/K pairs, Q -> q_out[t], K/V -> f16 cache at position pos0 + t
-  PG_QKV_SLOTS = 4,  // batched decode: token t is sequence t, at its own position and cache
-  PG_LOGITS = 5      // batched decode: logits row t, argmax key and finite flag of sequence t
+  PG_QKV = 3      // RoPE on Q/K pairs, Q -> q_out[t], K/V -> f16 cache at position pos0 + t
 };
 
 struct PrefillGemmArgs {
@@ -87,16 +84,6 @@ struct PrefillGemmArgs {
   __half* v_cache;
   const float2* rope;      // [ctx][head_dim/2]
   int32_t nq, nk, head_dim, pos0;
-  // PG_QKV_SLOTS / PG_LOGITS: sequence t's state and this layer's K/V rows
-  const SlotRef* slots;
-  int32_t n_eog;           // PG_LOGITS: ids excluded from the argmax
-  int64_t eog[kMaxEog];
-  // split K (grid.z > 1): super-block columns per split; each split's 128 x BN
-  // partial tile goes to part, and the split that finishes a tile last sums
-  // the partials in split order and runs the epilogue
-  int32_t k_chunk;
-  float* part;             // [m_tiles][n_tiles][splits][128][BN]
-  unsigned int* tile_cnt;  // [m_tiles][n_tiles], zero between launches
 };
 
 // ---- tcgen05 / TMA helpers ------------------------------------------------
@@ -220,19 +207,13 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   uint64_t* a_empty = a_full + kPgAStages;     // [kPgAStages] MMAs reading it finished
   uint64_t* tile_done = a_empty + kPgAStages;  // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_done + 1);
-  int* last_split = reinterpret_cast<int*>(tmem_slot + 1);
   float* xs_s = reinterpret_cast<float*>(smem + kPgSmemXs);  // row scales of this tile's tokens
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the column tiles of one weight tile are neighbours in launch order, so
   // its Q4_K bytes come from DRAM once and from L2 for the others
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  // this CTA's super-block columns [sb0, sb1) (all of K unless split)
-  const int splits = (int)gridDim.z;
-  const int sb0 = splits > 1 ? (int)blockIdx.z * a.k_chunk : 0;
-  const int sb1 = splits > 1 ? min(a.nb, sb0 + a.k_chunk) : a.nb;
-  const int kb0 = sb0 * (256 / kPgBK);
-  const int nkb = (sb1 - sb0) * (256 / kPgBK);  // K steps
+  const int nkb = a.nb * (256 / kPgBK);  // K steps
   if (threadIdx.x < BN / 2) {
     const int t = n_tile * (BN / 2) + threadIdx.x;
     xs_s[threadIdx.x] = t < a.n_tok ? a.xscale[t] : 0.0f;
@@ -266,7 +247,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
         const int s = kb % kPgBStages;
         if (kb >= kPgBStages) mbar_wait(&b_empty[s], ((kb / kPgBStages) - 1) & 1);
         mbar_arrive_expect_tx(&b_full[s], (uint32_t)kPgBTile);
-        tma_load_2d(sb + s * kPgBTile, &xs_map, (kb0 + kb) * kPgBK, n_tile * BN, &b_full[s]);
+        tma_load_2d(sb + s * kPgBTile, &xs_map, kb * kPgBK, n_tile * BN, &b_full[s]);
       }
     }
   } else if (warp == 1) {
@@ -312,16 +293,16 @@ __global__ void __launch_bounds__(kPgThreads, 1)
 #pragma unroll
       for (int j = 0; j < 8; ++j) nq[j] = row_live ? __ldg(qp + j) : z;
     };
-    fetch(sb0);
-    for (int sbk = sb0; sbk < sb1; ++sbk) {
+    fetch(0);
+    for (int sbk = 0; sbk < a.nb; ++sbk) {
       const uint4 hdr = nh;
       uint4 q[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) q[j] = nq[j];
-      if (sbk + 1 < sb1) fetch(sbk + 1);
+      if (sbk + 1 < a.nb) fetch(sbk + 1);
 #pragma unroll
       for (int chunk = 0; chunk < 4; ++chunk) {
-        const int kb = (sbk - sb0) * 4 + chunk, s = kb % kPgAStages;
+        const int kb = sbk * 4 + chunk, s = kb % kPgAStages;
         {
           const uint32_t k = 2u * (uint32_t)(chunk & 1);
           lc.sel = k | (5u << 4) | ((k + 1u) << 8) | (7u << 12);
@@ -370,50 +351,9 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     const bool row_ok = m < a.m_rows;
     constexpr int CW = kCols < 32 ? kCols : 32;    // columns per TMEM read
     constexpr int TPC = CW / 2;                    // tokens per TMEM read
-    const int prow = quad * 32 + lane;             // this lane's row of the tile
-    float* tile_part = nullptr;
-    if (splits > 1) {
-      // publish this split's partial tile; the last split to finish the
-      // tile runs the epilogue on the sum of all of them
-      tile_part = a.part + (size_t)(blockIdx.y * gridDim.x + n_tile) * splits * kPgBM * BN;
-      float* mine = tile_part + ((size_t)blockIdx.z * kPgBM + prow) * BN;
-      for (int c0 = cbeg; c0 < cbeg + kCols; c0 += CW) {
-        float v[CW];
-        tmem_ld_cols<CW>(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
-#pragma unroll
-        for (int i = 0; i < CW; i += 4)
-          *reinterpret_cast<float4*>(mine + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (threadIdx.x == 64) {
-        const unsigned int ticket = atomicAdd(&a.tile_cnt[blockIdx.y * gridDim.x + n_tile], 1u);
-        *last_split = ticket == (unsigned int)splits - 1u;
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-    }
-    const bool run_epi = splits == 1 || *last_split != 0;
-    if (run_epi && splits > 1) __threadfence();
-    for (int c0 = cbeg; run_epi && c0 < cbeg + kCols; c0 += CW) {
+    for (int c0 = cbeg; c0 < cbeg + kCols; c0 += CW) {
       float v[CW];
-      if (splits == 1) {
-        tmem_ld_cols<CW>(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
-      } else {
-        // the splits' partials summed in split order (deterministic)
-#pragma unroll
-        for (int i = 0; i < CW; ++i) v[i] = 0.0f;
-        for (int z = 0; z < splits; ++z) {
-          const float* pz = tile_part + ((size_t)z * kPgBM + prow) * BN + c0;
-#pragma unroll
-          for (int i = 0; i < CW; i += 4) {
-            const float4 f = __ldcg(reinterpret_cast<const float4*>(pz + i));
-            v[i] += f.x;
-            v[i + 1] += f.y;
-            v[i + 2] += f.z;
-            v[i + 3] += f.w;
-          }
-        }
-      }
+      tmem_ld_cols<CW>(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
       const int tb = (n_tile * BN + c0) / 2;  // first token of these column pairs
       float y[TPC];
 #pragma unroll
@@ -447,15 +387,12 @@ __global__ void __launch_bounds__(kPgThreads, 1)
             a.out[(size_t)t * a.ld_out + (m >> 1)] = __fmul_rn(sg, u);
           }
         }
-      } else if (EPI == PG_QKV || EPI == PG_QKV_SLOTS) {
+      } else if (EPI == PG_QKV) {
         const bool rope = m < a.nq + a.nk;  // Q and K rows (warp-uniform: head-aligned)
         const int kk = (m % a.head_dim) >> 1;
         int pos[TPC];
 #pragma unroll
-        for (int j = 0; j < TPC; ++j) {
-          if (EPI == PG_QKV) pos[j] = a.pos0 + tb + j;
-          else pos[j] = tb + j < a.n_tok ? a.slots[tb + j].st->cur_pos : 0;
-        }
+        for (int j = 0; j < TPC; ++j) pos[j] = a.pos0 + tb + j;
         float2 cs[TPC];
 #pragma unroll
         for (int j = 0; j < TPC; ++j)
@@ -466,8 +403,8 @@ __global__ void __launch_bounds__(kPgThreads, 1)
           const float y1 = __shfl_xor_sync(0xffffffffu, y[j], 1);
           const int t = tb + j;
           if (t < a.n_tok && row_ok) {
-            __half* kc = EPI == PG_QKV ? a.k_cache : a.slots[t].k;
-            __half* vc = EPI == PG_QKV ? a.v_cache : a.slots[t].v;
+            __half* kc = a.k_cache;
+            __half* vc = a.v_cache;
             if (rope) {
               // rope_norm pair (m even: first, odd: second) with host cos/sin
               const bool first = (m & 1) == 0;
@@ -481,34 +418,8 @@ __global__ void __launch_bounds__(kPgThreads, 1)
             }
           }
         }
-      } else {  // PG_LOGITS: top1_non_eog (src/cpu_oracle.rs:979-995) per sequence
-        bool eog = false;
-        for (int e = 0; e < a.n_eog; ++e) eog |= (a.eog[e] == (int64_t)m);
-#pragma unroll
-        for (int j = 0; j < TPC; ++j) {
-          const int t = tb + j;
-          const bool live = t < a.n_tok && row_ok;
-          if (live) a.out[(size_t)t * a.ld_out + m] = y[j];
-          // strict '>' from -inf: NaN and -inf never win, the lowest id wins ties
-          unsigned long long key = 0ull;
-          if (live && !eog && y[j] > -INFINITY)
-            key = ((unsigned long long)ordered_bits(y[j]) << 32) | (0xffffffffu - (uint32_t)m);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-            key = other > key ? other : key;
-          }
-          const bool bad = __any_sync(0xffffffffu, live && !isfinite(y[j]));
-          if (lane == 0 && t < a.n_tok) {
-            StepState* st = a.slots[t].st;
-            if (key) atomicMax(&st->argmax_key, key);
-            if (bad) atomicAnd(&st->finite, 0);
-          }
-        }
       }
     }
-    // every split has taken its ticket: the counter is free for the next launch
-    if (splits > 1 && run_epi && threadIdx.x == 64) a.tile_cnt[blockIdx.y * gridDim.x + n_tile] = 0u;
     tc_fence_before();
   }
   __syncthreads();
