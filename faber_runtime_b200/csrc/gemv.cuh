@@ -160,6 +160,59 @@ __device__ __forceinline__ float peer_sum1(const GemvArgs& a, int i, uint32_t e)
   return s;
 }
 
+// Tensor-parallel groups up to this size form the whole summed input in
+// every CTA (tp x n peer words read per CTA, no grid barrier); larger groups
+// sum one slice per CTA and publish it through a grid barrier.
+constexpr int kTpFullSum = 4;
+
+__device__ __forceinline__ ulonglong2 ld_peer2(const unsigned long long* p) {
+  ulonglong2 w;
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+  return w;
+}
+
+// x + the ranks' partials (rank order, as peer_sum1) of every element, into
+// xsum[n] in shared memory: 256 threads, element pairs, the words of 4
+// pairs per thread requested before any is checked.
+__device__ __forceinline__ void peer_full_sum(const GemvArgs& a, float* xsum, uint32_t e) {
+  constexpr int NT = kGemvThreads, kB = 4;
+  const int n = a.n_cols, n2 = n / 2, tid = threadIdx.x;
+  const uint32_t lim = peer_limit(a);
+  for (int base = 0; base < n2; base += kB * NT) {
+    ulonglong2 w[kB][kTpFullSum];
+    float2 xv[kB];
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int j = base + k * NT + tid;
+      if (j < n2) {
+        xv[k] = reinterpret_cast<const float2*>(a.x)[j];
+#pragma unroll
+        for (int p = 0; p < kTpFullSum; ++p)
+          if (p < a.tp) w[k][p] = ld_peer2(a.red + (size_t)p * n + 2 * j);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int j = base + k * NT + tid;
+      if (j >= n2) break;
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int p = 0; p < kTpFullSum; ++p) {
+        if (p >= a.tp) break;
+        const unsigned long long* wp = a.red + (size_t)p * n + 2 * j;
+        const float v0 = (uint32_t)(w[k][p].x >> 32) == e ? __uint_as_float((uint32_t)w[k][p].x)
+                                                           : peer_value(wp, e, lim);
+        const float v1 = (uint32_t)(w[k][p].y >> 32) == e ? __uint_as_float((uint32_t)w[k][p].y)
+                                                           : peer_value(wp + 1, e, lim);
+        s0 = p == 0 ? v0 : s0 + v0;
+        s1 = p == 0 ? v1 : s1 + v1;
+      }
+      xsum[2 * j] = xv[k].x + s0;
+      xsum[2 * j + 1] = xv[k].y + s1;
+    }
+  }
+}
+
 // Grid-wide barrier of a persistent grid (every CTA resident), thread 0 of
 // each CTA; sense-reversing, so the same two words serve every launch.
 // Bounded like the peer waits.
@@ -246,8 +299,10 @@ __device__ __forceinline__ int split_shift(float bound) {
 
 // Element i of the GEMV input before normalization (x, or x + x2).
 template <int PRO>
-__device__ __forceinline__ float4 load_x4(const GemvArgs& a, int i4) {
-  if (PRO == PRO_NORM_PEERS) return __ldcg(reinterpret_cast<const float4*>(a.x_sum_out) + i4);
+__device__ __forceinline__ float4 load_x4(const GemvArgs& a, int i4, const float* xsum) {
+  if (PRO == PRO_NORM_PEERS)
+    return xsum ? reinterpret_cast<const float4*>(xsum)[i4]
+                : __ldcg(reinterpret_cast<const float4*>(a.x_sum_out) + i4);
   float4 v = reinterpret_cast<const float4*>(a.x)[i4];
   if (PRO == PRO_NORM_RES) {
     const float4 u = reinterpret_cast<const float4*>(a.x2)[i4];
@@ -257,9 +312,9 @@ __device__ __forceinline__ float4 load_x4(const GemvArgs& a, int i4) {
 }
 
 template <int PRO>
-__device__ __forceinline__ float load_x1(const GemvArgs& a, int i) {
+__device__ __forceinline__ float load_x1(const GemvArgs& a, int i, const float* xsum) {
   if (PRO == PRO_NORM_RES) return a.x[i] + a.x2[i];
-  if (PRO == PRO_NORM_PEERS) return __ldcg(a.x_sum_out + i);
+  if (PRO == PRO_NORM_PEERS) return xsum ? xsum[i] : __ldcg(a.x_sum_out + i);
   return a.x[i];
 }
 
@@ -297,16 +352,27 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
   constexpr int NT = kGemvThreads;
   const int n = a.n_cols;
   const int tid = threadIdx.x;
+  // PRO_NORM_PEERS, small groups: the whole summed input in shared memory
+  // (the x staging area, free until the split below; CTA 0 publishes it)
+  float* xsum = nullptr;
   if (PRO == PRO_NORM_PEERS) {
-    // this CTA's slice of x + sum of the ranks' partials, then every slice
     const uint32_t e = tp_epoch(a);
-    const int per = (n + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int i1 = min(n, ((int)blockIdx.x + 1) * per);
-    for (int i = (int)blockIdx.x * per + tid; i < i1; i += NT)
-      a.x_sum_out[i] = a.x[i] + peer_sum1(a, i, e);
-    cbar<NAMED>();
-    if (tid == 0) grid_barrier(a.grid_bar, peer_limit(a));
-    cbar<NAMED>();
+    // (only where the staging below takes its vectorized one-batch path,
+    // which keeps every value in registers before the split overwrites xsum)
+    if (a.tp <= kTpFullSum && n % 4 == 0 && n / 4 <= NT * 8 && aligned16(a.x) && aligned16(a.norm_w)) {
+      xsum = reinterpret_cast<float*>(xh);
+      peer_full_sum(a, xsum, e);
+      cbar<NAMED>();
+    } else {
+      // this CTA's slice of x + sum of the ranks' partials, then every slice
+      const int per = (n + (int)gridDim.x - 1) / (int)gridDim.x;
+      const int i1 = min(n, ((int)blockIdx.x + 1) * per);
+      for (int i = (int)blockIdx.x * per + tid; i < i1; i += NT)
+        a.x_sum_out[i] = a.x[i] + peer_sum1(a, i, e);
+      cbar<NAMED>();
+      if (tid == 0) grid_barrier(a.grid_bar, peer_limit(a));
+      cbar<NAMED>();
+    }
   }
   const bool vec = (n % 4 == 0) && aligned16(a.x) &&
                    (PRO == PRO_PLAIN || aligned16(a.norm_w)) &&
@@ -328,7 +394,7 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
       for (int k = 0; k < kXB; ++k) {
         const int i4 = base + tid + k * NT;
         if (i4 < n4) {
-          v[k] = load_x4<PRO>(a, i4);
+          v[k] = load_x4<PRO>(a, i4, xsum);
           if (PRO != PRO_PLAIN) w[k] = reinterpret_cast<const float4*>(a.norm_w)[i4];
         }
       }
@@ -349,7 +415,7 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
     }
   } else {
     for (int i = tid; i < n; i += NT) {
-      const float v = load_x1<PRO>(a, i);
+      const float v = load_x1<PRO>(a, i, xsum);
       if (PRO != PRO_PLAIN) {
         ss += (double)v * (double)v;
         mx = fmaxf(mx, fabsf(v * a.norm_w[i]));
@@ -387,7 +453,7 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
         for (int k = 0; k < kXB; ++k) {
           const int i4 = base + tid + k * NT;
           if (i4 < n4) {
-            v[k] = load_x4<PRO>(a, i4);
+            v[k] = load_x4<PRO>(a, i4, xsum);
             if (PRO != PRO_PLAIN) w[k] = reinterpret_cast<const float4*>(a.norm_w)[i4];
           }
         }
@@ -401,7 +467,8 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
           y = make_float4(norm1<PRO>(v[k].x, scale, w[k].x), norm1<PRO>(v[k].y, scale, w[k].y),
                           norm1<PRO>(v[k].z, scale, w[k].z), norm1<PRO>(v[k].w, scale, w[k].w));
         if (cta0) {
-          if (PRO == PRO_NORM_RES) reinterpret_cast<float4*>(a.x_sum_out)[i4] = v[k];
+          if (PRO == PRO_NORM_RES || (PRO == PRO_NORM_PEERS && xsum))
+            reinterpret_cast<float4*>(a.x_sum_out)[i4] = v[k];
           if (PRO != PRO_PLAIN && a.x_norm_out) reinterpret_cast<float4*>(a.x_norm_out)[i4] = y;
         }
         if (PERM) split_store(y.x, y.z, y.y, y.w, in_s, xh, xl, xs_index(kXPad + 4 * i4));
@@ -410,10 +477,10 @@ __device__ float stage_x(const GemvArgs& a, __half* xh, __half* xl, double* redd
     }
   } else {
     for (int i = tid; i < n; i += NT) {
-      const float v = load_x1<PRO>(a, i);
+      const float v = load_x1<PRO>(a, i, xsum);
       const float y = PRO == PRO_PLAIN ? v : norm1<PRO>(v, scale, a.norm_w[i]);
       if (cta0) {
-        if (PRO == PRO_NORM_RES) a.x_sum_out[i] = v;
+        if (PRO == PRO_NORM_RES || (PRO == PRO_NORM_PEERS && xsum)) a.x_sum_out[i] = v;
         if (PRO != PRO_PLAIN && a.x_norm_out) a.x_norm_out[i] = y;
       }
       const float sv = y * in_s;

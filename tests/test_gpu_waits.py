@@ -77,8 +77,9 @@ def _exchange_case(cuda, rows=2048, cols=4096, tp=3, seed=9):
     return w, parts, x_sum, want, call
 
 
-def test_exchange_gemv_matches_the_oracle_when_every_word_arrived(cuda):
-    w, parts, x_sum, want, call = _exchange_case(cuda)
+@pytest.mark.parametrize("tp", [2, 3, 8])  # every CTA sums all (<= 4) / slices + grid barrier (8)
+def test_exchange_gemv_matches_the_oracle_when_every_word_arrived(cuda, tp):
+    w, parts, x_sum, want, call = _exchange_case(cuda, tp=tp)
     got_sum, y = call(_words(parts, 7), 7, 0)
     assert np.array_equal(got_sum.view(np.uint32), x_sum.view(np.uint32))
     within(y, want)
