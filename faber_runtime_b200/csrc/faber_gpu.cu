@@ -603,7 +603,10 @@ __attribute__((visibility("default"))) FaberRtStatusV1 faber_gpu_v2_q4k_gemv(
     GemvArgs a = t->t.args();
     a.x = x;
     a.out = y;
-    launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, as_stream(stream), false);
+    // programmatic dependent launch, as in the decode step: the producer
+    // streams weights while the previous kernel finishes; every read of x
+    // and write of y waits for that kernel's completion
+    launch_gemv<WL_TILED, PRO_PLAIN, EPI_STORE>(a, as_stream(stream), true);
   });
 }
 
