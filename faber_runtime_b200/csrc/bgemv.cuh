@@ -32,7 +32,7 @@ namespace faber {
 enum BgemvEpilogue : int { BG_STORE = 0, BG_RESID = 1, BG_SWIGLU = 2, BG_QKV = 3, BG_LOGITS = 4 };
 
 constexpr int kBgMaxSeq = 16;
-constexpr int kBgStages = 3;
+constexpr int kBgStages = 4;
 constexpr int kBgParts = 2;  // partial-tile buffers between the warps and the epilogue warp
 constexpr size_t kBgSmemMax = 227 * 1024;
 
@@ -66,14 +66,22 @@ struct BgMeta {
 
 struct BgLayout {
   size_t ring, xs, part, meta, bars, total;
-  int row_halves;  // padded x row length (halves); rows start 64 bytes apart mod 128
+  int row_halves;  // x row stride (halves): rows start 16 bytes apart mod 128
 };
+
+// Shared-memory position (halves) of element j (a multiple of 8) of a staged
+// x row: its 16-byte chunk k moves to k ^ (2 * ((k >> 3) & 3)), so the four
+// lane groups t of one B-fragment load (chunks 8t apart) use four different
+// 16-byte bank slots, and the next row (16 bytes on) the other four.
+__host__ __device__ __forceinline__ int bg_swz(int j) {
+  const int k = j >> 3;
+  return (k ^ (((k >> 3) & 3) << 1)) << 3;
+}
 
 __host__ __device__ inline BgLayout bg_layout(int slab_sb, int B) {
   BgLayout L;
   const int n = slab_sb * 256;
-  int rh = n + (n >> 3);
-  if ((rh * 2) % 128 != 64) rh += ((64 - (rh * 2) % 128) + 128) % 128 / 2;
+  const int rh = n + 8;  // 2n is a multiple of 512: rows 16 bytes apart mod 128
   L.row_halves = rh;
   L.ring = 0;
   L.xs = (size_t)kBgStages * kStageBytes;
@@ -96,9 +104,11 @@ __host__ inline int bg_slab_sb(int nb, int B) {
 
 // One item for NB column blocks: the weight fragment of each quant word is
 // formed once and multiplied into every block's accumulators.
+// xlo / xhi: this lane's swizzled x offsets of the item's low and high runs;
+// tb = t & 1 swaps the two 16-element halves (pp) of odd lane groups.
 template <int NB>
 __device__ __forceinline__ void bq4_item(const uint8_t* hdr, const uint8_t* qnt,
-                                         const __half* const (&xrow)[NB], int xlo, int xhi,
+                                         const __half* const (&xrow)[NB], int xlo, int xhi, int tb,
                                          float (&acc)[NB][2][4], const ItemConst& ic) {
   using G = ItemGeom<WL_TILED>;
   const uint4 hA = *reinterpret_cast<const uint4*>(hdr);
@@ -114,8 +124,8 @@ __device__ __forceinline__ void bq4_item(const uint8_t* hdr, const uint8_t* qnt,
       uint4 xl[NB], xh[NB];
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
-        xl[c] = *reinterpret_cast<const uint4*>(xrow[c] + xlo + 16 * pp + 8 * ih);
-        xh[c] = *reinterpret_cast<const uint4*>(xrow[c] + xhi + 16 * pp + 8 * ih);
+        xl[c] = *reinterpret_cast<const uint4*>(xrow[c] + xlo + 16 * (pp ^ tb) + 8 * ih);
+        xh[c] = *reinterpret_cast<const uint4*>(xrow[c] + xhi + 16 * (pp ^ tb) + 8 * ih);
       }
 #pragma unroll
       for (int i2 = 0; i2 < 2; ++i2) {
@@ -395,7 +405,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) bgemv_kernel(const BgemvArgs 
           pv.y = __byte_perm(v[k].x, v[k].y, 0x7632);  // e1, e3
           pv.z = __byte_perm(v[k].z, v[k].w, 0x5410);
           pv.w = __byte_perm(v[k].z, v[k].w, 0x7632);
-          *reinterpret_cast<uint4*>(xsl + (size_t)c * L.row_halves + xs_index(j)) = pv;
+          *reinterpret_cast<uint4*>(xsl + (size_t)c * L.row_halves + bg_swz(j)) = pv;
         }
       }
     }
@@ -412,7 +422,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) bgemv_kernel(const BgemvArgs 
   using Gm = ItemGeom<WL_TILED>;
   const int off_h = warp * kTileItemBytes + Gm::kHead * g;
   const int off_q = warp * kTileItemBytes + Gm::kQuant0 + Gm::kQuantRow * g + 32 * t;
-  constexpr int kRoundHalves = kConsumerWarps * 256 + ((kConsumerWarps * 256) >> 3);
+  constexpr int kRoundHalves = kConsumerWarps * 256;  // 8 super-blocks: the swizzle repeats every 32 chunks
+  const int tb = t & 1;
   int s = 0, it = 0;
   uint32_t ph = 0;
   for (int tile = gi; tile < a.n_tiles; tile += gs, ++it) {
@@ -421,12 +432,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1) bgemv_kernel(const BgemvArgs 
     for (int c = 0; c < NB; ++c)
 #pragma unroll
       for (int h = 0; h < 2; ++h) acc[c][h][0] = acc[c][h][1] = acc[c][h][2] = acc[c][h][3] = 0.f;
-    int xlo = xs_index(warp * 256 + 64 * t), xhi = xs_index(warp * 256 + 64 * t + 32);
+    // element 64t (+32) of this warp's first item, swizzled: chunk 8t (+4)
+    // of the super-block, whose bits 1-2 flip by 2t
+    int xlo = warp * 256 + 64 * t + 32 * (t >> 1), xhi = warp * 256 + 64 * t + 32 * ((t >> 1) ^ 1);
     for (int r = 0, b = warp; r < R; ++r, b += kConsumerWarps) {
       mbar_wait(&full[s], ph);
       if (b < S) {
         const uint8_t* slot = ring + (size_t)s * kStageBytes;
-        bq4_item<NB>(slot + off_h, slot + off_q, xrow, xlo, xhi, acc, ic);
+        bq4_item<NB>(slot + off_h, slot + off_q, xrow, xlo, xhi, tb, acc, ic);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
