@@ -116,8 +116,11 @@ def test_repack_rejects_bad_byte_length(cuda):
     assert e.value.code == 1
 
 
+# 4096 rows: fewer tiles than CTA slots, every tile split between CTAs;
+# 11008 rows: two whole-tile waves and a split tail; 4752 x 256 and
+# 4800 x 512: one wave and a tail of fewer items than CTAs
 GEMV_SHAPES = [(4096, 4096), (16, 256), (17, 512), (2 * 1408, 512), (512, 1408), (11008, 4096),
-               (4096, 11008), (100, 1024)]
+               (4096, 11008), (100, 1024), (4752, 256), (4800, 512)]
 
 
 @pytest.mark.parametrize("rows,cols", GEMV_SHAPES)
