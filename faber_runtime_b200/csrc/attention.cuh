@@ -49,6 +49,7 @@ struct AttnArgs {
   // K/V rows; q/ctx, part and counters advance by these strides per sequence
   const SlotRef* slots;
   int32_t slot_q_stride, slot_part_stride, slot_counter_stride;
+  int32_t cache_rows;      // rows of k / v (the TMA-streamed kernel's tensor maps)
 };
 
 // The arguments of sequence blockIdx.z of a batched launch (identity for a
@@ -90,6 +91,7 @@ template <> struct KvVec<4> {
   }
   // the row the preceding kernel wrote: coherent load after the wait
   __device__ __forceinline__ void load(const __half* p) { u = *reinterpret_cast<const uint2*>(p); }
+  __device__ __forceinline__ void load_smem(const void* p) { u = *reinterpret_cast<const uint2*>(p); }
   __device__ __forceinline__ void to_float(float (&f)[4]) const {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
@@ -106,6 +108,7 @@ template <> struct KvVec<2> {
     asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(u) : "l"(p));
   }
   __device__ __forceinline__ void load(const __half* p) { u = *reinterpret_cast<const uint32_t*>(p); }
+  __device__ __forceinline__ void load_smem(const void* p) { u = *reinterpret_cast<const uint32_t*>(p); }
   __device__ __forceinline__ void to_float(float (&f)[2]) const {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u));
     f[0] = a.x;
@@ -226,6 +229,93 @@ __device__ __forceinline__ void kv_consume(const KvGroup<DPL>& g, int j0, int n_
   __syncwarp();
 }
 
+// The end of a split CTA (4 warps, threads 0-127, sync() a barrier over
+// them): combine the warps' (max, sum, context) into the split's partial,
+// and let the last CTA of the kv head (atomic ticket) merge all splits in
+// split order.
+template <int HD, int R, class Sync>
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, int kh, int split, int active, int ratio, int warp,
+                                            int lane, const float (&m)[R], const float (&l)[R],
+                                            const float (&acc)[R][HD / 32], float (&wstat)[kAttnWarps][R][2],
+                                            float (&red)[kAttnWarps][R][HD], int* is_last, Sync sync) {
+  constexpr int DPL = HD / 32;
+  // combine the warps into this split's partial (max, sum, context)
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (r >= ratio) break;
+    if (lane == 0) {
+      wstat[warp][r][0] = m[r];
+      wstat[warp][r][1] = l[r];
+    }
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) red[warp][r][lane * DPL + d] = acc[r][d];
+  }
+  sync();
+  const int stride = HD + 2;
+  for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
+    const int r = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wstat[w][r][0]);
+    float L = 0.0f, s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float f = wstat[w][r][0] == -INFINITY ? 0.0f : expf(wstat[w][r][0] - M);
+      L = fmaf(wstat[w][r][1], f, L);
+      s = fmaf(red[w][r][d], f, s);
+    }
+    float* pp = a.part + ((size_t)(kh * ratio + r) * a.max_splits + split) * stride;
+    pp[2 + d] = s;
+    if (d == 0) {
+      pp[0] = M;
+      pp[1] = L;
+    }
+  }
+  // the last CTA of this kv head merges all splits in split order
+  __threadfence();
+  sync();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(&a.counters[kh], 1);
+    *is_last = (ticket == active - 1);
+  }
+  sync();
+  if (!*is_last) return;
+  __threadfence();
+  // One pass in split order, kAttnMergeBatch splits' loads in flight at a
+  // time: the running (max, sum, context) is rescaled to each batch's max.
+  for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
+    const int r = idx / HD, d = idx % HD;
+    const float* base = a.part + (size_t)(kh * ratio + r) * a.max_splits * stride;
+    float M = -INFINITY, L = 0.0f, acc_d = 0.0f;
+    for (int s0 = 0; s0 < active; s0 += kAttnMergeBatch) {
+      float ms[kAttnMergeBatch], ls[kAttnMergeBatch], vs[kAttnMergeBatch];
+#pragma unroll
+      for (int u = 0; u < kAttnMergeBatch; ++u) {
+        const bool ok = s0 + u < active;
+        const float* p = base + (size_t)(s0 + u) * stride;
+        ms[u] = ok ? __ldcg(p) : -INFINITY;
+        ls[u] = ok ? __ldcg(p + 1) : 0.0f;
+        vs[u] = ok ? __ldcg(p + 2 + d) : 0.0f;
+      }
+      float mb = M;  // every split holds a valid row, so mb is finite from here
+#pragma unroll
+      for (int u = 0; u < kAttnMergeBatch; ++u) mb = fmaxf(mb, ms[u]);
+      const float c = expf(M - mb);
+      L *= c;
+      acc_d *= c;
+#pragma unroll
+      for (int u = 0; u < kAttnMergeBatch; ++u) {
+        const float f = expf(ms[u] - mb);  // 0 for the padding entries
+        L = fmaf(ls[u], f, L);
+        acc_d = fmaf(vs[u], f, acc_d);
+      }
+      M = mb;
+    }
+    a.ctx[(size_t)(kh * ratio + r) * HD + d] = acc_d / L;
+  }
+  if (threadIdx.x == 0) a.counters[kh] = 0;
+}
+
 template <int HD, int R>
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnArgs a0) {
   const AttnArgs a = slot_args(a0);
@@ -284,81 +374,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
       kv_consume<DPL, R>(gb, jb, n_kv, ratio, a.scale, qv, m, l, acc, pw, lane);
     }
   }
-  // combine the warps into this split's partial (max, sum, context)
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    if (r >= ratio) break;
-    if (lane == 0) {
-      wstat[warp][r][0] = m[r];
-      wstat[warp][r][1] = l[r];
-    }
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) red[warp][r][lane * DPL + d] = acc[r][d];
-  }
-  __syncthreads();
-  const int stride = HD + 2;
-  for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
-    const int r = idx / HD, d = idx % HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wstat[w][r][0]);
-    float L = 0.0f, s = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = wstat[w][r][0] == -INFINITY ? 0.0f : expf(wstat[w][r][0] - M);
-      L = fmaf(wstat[w][r][1], f, L);
-      s = fmaf(red[w][r][d], f, s);
-    }
-    float* pp = a.part + ((size_t)(kh * ratio + r) * a.max_splits + split) * stride;
-    pp[2 + d] = s;
-    if (d == 0) {
-      pp[0] = M;
-      pp[1] = L;
-    }
-  }
-  // the last CTA of this kv head merges all splits in split order
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ticket = atomicAdd(&a.counters[kh], 1);
-    is_last = (ticket == active - 1);
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  // One pass in split order, kAttnMergeBatch splits' loads in flight at a
-  // time: the running (max, sum, context) is rescaled to each batch's max.
-  for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
-    const int r = idx / HD, d = idx % HD;
-    const float* base = a.part + (size_t)(kh * ratio + r) * a.max_splits * stride;
-    float M = -INFINITY, L = 0.0f, acc_d = 0.0f;
-    for (int s0 = 0; s0 < active; s0 += kAttnMergeBatch) {
-      float ms[kAttnMergeBatch], ls[kAttnMergeBatch], vs[kAttnMergeBatch];
-#pragma unroll
-      for (int u = 0; u < kAttnMergeBatch; ++u) {
-        const bool ok = s0 + u < active;
-        const float* p = base + (size_t)(s0 + u) * stride;
-        ms[u] = ok ? __ldcg(p) : -INFINITY;
-        ls[u] = ok ? __ldcg(p + 1) : 0.0f;
-        vs[u] = ok ? __ldcg(p + 2 + d) : 0.0f;
-      }
-      float mb = M;  // every split holds a valid row, so mb is finite from here
-#pragma unroll
-      for (int u = 0; u < kAttnMergeBatch; ++u) mb = fmaxf(mb, ms[u]);
-      const float c = expf(M - mb);
-      L *= c;
-      acc_d *= c;
-#pragma unroll
-      for (int u = 0; u < kAttnMergeBatch; ++u) {
-        const float f = expf(ms[u] - mb);  // 0 for the padding entries
-        L = fmaf(ls[u], f, L);
-        acc_d = fmaf(vs[u], f, acc_d);
-      }
-      M = mb;
-    }
-    a.ctx[(size_t)(kh * ratio + r) * HD + d] = acc_d / L;
-  }
-  if (threadIdx.x == 0) a.counters[kh] = 0;
+  attn_finish<HD, R>(a, kh, split, active, ratio, warp, lane, m, l, acc, wstat, red, &is_last,
+                     [] { __syncthreads(); });
 }
 
 }  // namespace faber

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "attention_stream.cuh"
 #include "bgemv.cuh"
 #include "prefill.cuh"
 
@@ -241,10 +242,20 @@ void launch_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pd
 
 // Decode attention of a step: grouped heads (ratio 3..8) on the tensor cores,
 // one wave of CTAs (kv heads x sequences x splits, the split count within the
-// session's partial buffer); other ratios on the CUDA-core kernel.
+// session's partial buffer); one or two query heads per kv head of a single
+// sequence on the TMA-streamed kernel; batched sequences of those ratios on
+// the register-streamed CUDA-core kernel.
 template <int HD>
 void launch_decode_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pdl) {
   const int ratio = a.n_heads / a.n_kv_heads;
+  if (ratio <= 2 && !a.slots && a.cache_rows > 0) {
+    const int splits = attention_stream_splits(device_info().sms, (int)grid.x, (int)grid.y);
+    if (ratio == 1)
+      launch_attention_stream<HD, 1>(a, (int)grid.x, splits, stream, pdl);
+    else
+      launch_attention_stream<HD, 2>(a, (int)grid.x, splits, stream, pdl);
+    return;
+  }
   if (ratio < 3 || ratio > 8) {
     launch_attention<HD>(a, grid, stream, pdl);
     return;
@@ -908,6 +919,7 @@ inline void enqueue_push(SessionState& S, bool pdl) {
       a.head_dim = hd;
       a.max_splits = S.max_splits;
       a.scale = 1.0f / sqrtf((float)hd);
+      a.cache_rows = S.max_ctx;
       const dim3 grid(M.Hkvl, S.max_splits);
       if (hd == 128)
         launch_decode_attention<128>(a, grid, S.stream, pdl);
@@ -1131,23 +1143,6 @@ inline bool prefill_supported(const ModelState& M) {
   const FaberModelConfigV1& c = M.cfg;
   const uint32_t nq = (uint32_t)M.Hl * c.head_dim;
   return M.tp == 1 && M.all_q4k && c.d_model % 256 == 0 && nq % 256 == 0 && M.Fl % 256 == 0;
-}
-
-using TmapEncode = PFN_cuTensorMapEncodeTiled_v12000;
-
-inline TmapEncode tmap_encoder() {
-  static TmapEncode fn = nullptr;
-  static std::mutex mu;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    FABER_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
-    require(p != nullptr && q == cudaDriverEntryPointSuccess, FABER_STATUS_UNSUPPORTED,
-            "cuTensorMapEncodeTiled is not available");
-    fn = reinterpret_cast<TmapEncode>(p);
-  }
-  return fn;
 }
 
 // Tensor map over the split activations [rows][K] f16: 64 x 256 boxes with the

@@ -191,6 +191,35 @@ def test_7b_shape_two_layers_over_prefix(cuda):
     assert len(drun) == n_prefix + 4
 
 
+@pytest.mark.parametrize("heads,kv_heads,head_dim,n_prefix", [
+    (8, 8, 128, 9001),   # ratio 1: six 32-position tiles per split CTA, the 4-stage ring wraps
+    (16, 8, 64, 8190),   # ratio 2: five tiles per split CTA, ragged last tile
+])
+def test_streamed_attention_over_long_prefix(cuda, heads, kv_heads, head_dim, n_prefix):
+    """One and two query heads per kv head over a long installed K/V prefix:
+    the TMA-streamed decode attention (each split CTA several 32-position
+    tiles through its ring, the tile holding the step's own row requested
+    after the dependency wait) gives the oracle's logits."""
+    import oracle as o
+    from faber_runtime_b200 import ForwardRun, ModelConfig, synth
+    cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=heads, n_kv_heads=kv_heads, head_dim=head_dim,
+                      ffn=2816, vocab=4096, tied_head=False, rope_theta=500000.0, name="stream-attn")
+    om, dm, _ = build_pair(cfg, 31, norms="random")
+    span = kv_heads * head_dim
+    orun = o.OracleRun(om, n_prefix + 8)
+    drun = ForwardRun(dm, context_length=n_prefix + 8)
+    for layer in range(cfg.n_layers):
+        k = synth.normal(31, 3000 + layer, n_prefix * span, 0.0, 2.0)
+        v = synth.normal(31, 4000 + layer, n_prefix * span, 0.0, 2.0)
+        orun.set_prefix(layer, k, v, n_prefix)
+        drun.set_prefix(layer, k, v, n_prefix)
+    for t in synth.tokens(31, 6, 4, cfg.vocab):
+        orun.push_token(int(t))
+        drun.push_token(int(t))
+        within(drun.position_logits(), orun.position_logits())
+    assert len(drun) == n_prefix + 4
+
+
 def test_70b_shape_one_layer_over_prefix(cuda):
     """The 70B shape at full width (d 8192, 64/8 heads of 128, FFN 28672 =
     112 super-blocks, vocab 128256) cut to one layer, over an installed
