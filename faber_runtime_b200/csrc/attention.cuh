@@ -22,6 +22,8 @@
 //     order, so results do not depend on CTA timing.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -50,6 +52,9 @@ struct AttnArgs {
   const SlotRef* slots;
   int32_t slot_q_stride, slot_part_stride, slot_counter_stride;
   int32_t cache_rows;      // rows of k / v (the TMA-streamed kernel's tensor maps)
+  // batched launches of the TMA-streamed kernel: this layer's K and V tensor
+  // maps of every sequence, [sequence][2], in device memory
+  const CUtensorMap* kvmaps;
 };
 
 // The arguments of sequence blockIdx.z of a batched launch (identity for a
@@ -229,27 +234,13 @@ __device__ __forceinline__ void kv_consume(const KvGroup<DPL>& g, int j0, int n_
   __syncwarp();
 }
 
-// The end of a split CTA (4 warps, threads 0-127, sync() a barrier over
-// them): combine the warps' (max, sum, context) into the split's partial,
+// Combine the 4 warps' stashed (max, sum, context) into the split's partial,
 // and let the last CTA of the kv head (atomic ticket) merge all splits in
-// split order.
+// split order. Threads 0-127 take part; sync() is a barrier over them.
 template <int HD, int R, class Sync>
-__device__ __forceinline__ void attn_finish(const AttnArgs& a, int kh, int split, int active, int ratio, int warp,
-                                            int lane, const float (&m)[R], const float (&l)[R],
-                                            const float (&acc)[R][HD / 32], float (&wstat)[kAttnWarps][R][2],
-                                            float (&red)[kAttnWarps][R][HD], int* is_last, Sync sync) {
-  constexpr int DPL = HD / 32;
-  // combine the warps into this split's partial (max, sum, context)
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    if (r >= ratio) break;
-    if (lane == 0) {
-      wstat[warp][r][0] = m[r];
-      wstat[warp][r][1] = l[r];
-    }
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) red[warp][r][lane * DPL + d] = acc[r][d];
-  }
+__device__ __forceinline__ void attn_merge(const AttnArgs& a, int kh, int split, int active, int ratio,
+                                           const float (&wstat)[kAttnWarps][R][2],
+                                           const float (&red)[kAttnWarps][R][HD], int* is_last, Sync sync) {
   sync();
   const int stride = HD + 2;
   for (int idx = threadIdx.x; idx < ratio * HD; idx += kAttnThreads) {
@@ -314,6 +305,28 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int kh, int split
     a.ctx[(size_t)(kh * ratio + r) * HD + d] = acc_d / L;
   }
   if (threadIdx.x == 0) a.counters[kh] = 0;
+}
+
+// The end of a split CTA (4 warps, threads 0-127, sync() a barrier over
+// them): each warp stashes its (max, sum, context), then attn_merge.
+template <int HD, int R, class Sync>
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, int kh, int split, int active, int ratio, int warp,
+                                            int lane, const float (&m)[R], const float (&l)[R],
+                                            const float (&acc)[R][HD / 32], float (&wstat)[kAttnWarps][R][2],
+                                            float (&red)[kAttnWarps][R][HD], int* is_last, Sync sync) {
+  constexpr int DPL = HD / 32;
+  // stash this warp's state
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (r >= ratio) break;
+    if (lane == 0) {
+      wstat[warp][r][0] = m[r];
+      wstat[warp][r][1] = l[r];
+    }
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) red[warp][r][lane * DPL + d] = acc[r][d];
+  }
+  attn_merge<HD, R>(a, kh, split, active, ratio, wstat, red, is_last, sync);
 }
 
 template <int HD, int R>

@@ -1,25 +1,28 @@
-// attention_stream.cuh — decode attention for one or two query heads per kv
-// head (the Llama-2-7B step), K/V tiles streamed into shared memory by TMA
-// (attention_gqa, src/cpu_oracle.rs:711-792, for one query row).
+// attention_stream.cuh — decode attention for up to two query heads per kv
+// head (the Llama-2-7B step is one), K/V tiles streamed into shared memory by
+// TMA, scores and context on the tensor cores (attention_gqa,
+// src/cpu_oracle.rs:711-792, for one query row).
 //
-// The register-streamed kernel (attention.cuh) keeps one or two 8-row groups
-// per warp in flight, too few bytes per SM to reach HBM rate on a launch of a
-// few microseconds. Here a producer warp moves whole 32-position tiles of K
-// and V (32 x head_dim f16 each, one 2D tensor copy apiece) into a 4-stage
-// shared ring, so every CTA has up to 64 KB requested at once, and three CTAs
-// share an SM:
-//   * grid (kv heads, splits), splits chosen so the grid is about one wave of
-//     three CTAs per SM; CTA (kh, split) covers an equal share of the
-//     context's 32-position groups, in order;
-//   * tiles whose rows all precede the step's own position were written by
-//     earlier steps: the producer requests them before the programmatic-
-//     dependency wait, so they stream during the tail of the QKV kernel; the
-//     tile holding row cur is requested after the wait;
-//   * each consumer warp copies its 8 rows of a stage into registers,
-//     releases the slot and scores them exactly as the register-streamed
-//     kernel does (per-lane partial dots, butterfly reduction, online softmax
-//     per warp), then the warps and splits merge in the same fixed order
-//     (attn_finish), so results do not depend on CTA timing.
+//   * grid (kv heads, splits, sequences), three CTAs per SM, the split count
+//     chosen from the launch's shape (attention_stream_splits); CTA (kh,
+//     split) covers an equal share of the context's 16-key groups, in order.
+//     A single sequence's tensor maps are kernel parameters, a batch's are
+//     read from a device array (one K and one V map per sequence);
+//   * a producer warp moves each group's K and V (16 keys x head_dim f16,
+//     64-dim halves with the 128-byte swizzle) into an 8-stage ring with 2D
+//     tensor copies, up to 64 KB per CTA in flight. Groups whose keys all
+//     precede the step's own position were written by earlier steps: they
+//     are requested before the programmatic-dependency wait, so they stream
+//     during the tail of the QKV kernel; the group holding row cur after it;
+//   * consumer warp w takes groups w, w + 4, ... Each query head is split
+//     exactly into f16 hi and lo rows (per-head power-of-two scale) of the
+//     MMA A operand: S = Q K^T on m16n8k16 (8 k-steps per 16 keys at head_dim
+//     128), score = (S_hi + S_lo) * scale; an online softmax per warp; the
+//     probabilities, split into hi/lo rows the same way, multiply V (the
+//     score accumulator's layout is the A fragment's), so both products keep
+//     about f32 accuracy;
+//   * the warps and then the splits merge in a fixed order (attn_merge), so
+//     results do not depend on CTA timing.
 #pragma once
 
 #include <cudaTypedefs.h>
@@ -29,29 +32,39 @@
 
 #include "attention.cuh"
 #include "gemv.cuh"
+#include "prefill.cuh"
 
 namespace faber {
 
-constexpr int kAsRows = 32;                          // positions per stage (8 per consumer warp)
-constexpr int kAsStages = 4;
+constexpr int kAsKeys = 16;                          // keys per stage: one k-step of P V
+constexpr int kAsStages = 8;
 constexpr int kAsConsumers = kAttnWarps;             // 4 consumer warps
 constexpr int kAsThreads = (kAsConsumers + 1) * 32;  // + the producer warp
 constexpr int kAsCtasPerSm = 3;
-static_assert(kAsRows == kAttnRows * kAsConsumers, "one 8-row slice per consumer warp");
+constexpr int kAsMaxRatio = 2;
 
 template <int HD>
 struct AsLayout {
-  static constexpr int kTile = kAsRows * HD * 2;  // bytes of one K (or V) tile
+  static constexpr int kHalves = HD / 64;            // 64-dim halves: 128-byte rows
+  static constexpr int kHalf = kAsKeys * 128;        // one half of a 16-row tile
+  static constexpr int kTile = kHalves * kHalf;      // one K (or V, or Q) tile
   static constexpr int kStage = 2 * kTile;
-  static constexpr int kBarOff = kAsStages * kStage;
-  static constexpr int kBytes = kBarOff + 2 * kAsStages * 8;
+  static constexpr int kQOff = kAsStages * kStage;   // Q hi/lo rows, same layout
+  static constexpr int kBarOff = kQOff + kTile;
+  static constexpr int kBytes = kBarOff + 2 * kAsStages * 8 + 1024;  // + alignment slack
 };
 
-__device__ __forceinline__ void tma_load_tile(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+// Byte offset of (row, 16-byte chunk) in a 16-row tile stored as 64-dim
+// halves of 128-byte rows with the 128-byte swizzle (chunk ^ row % 8).
+__device__ __forceinline__ uint32_t as_off(int row, int chunk) {
+  return (uint32_t)((chunk >> 3) * (kAsKeys * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void tma_load_tile(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
                                               uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
@@ -60,17 +73,21 @@ __device__ __forceinline__ void consumer_bar_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kAsConsumers * 32) : "memory");
 }
 
-template <int HD, int R>
-__global__ void __launch_bounds__(kAsThreads) attention_stream_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                                      const __grid_constant__ CUtensorMap vmap,
-                                                                      const AttnArgs a) {
+template <int HD>
+__global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
+    attention_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                            const AttnArgs a0) {
+  const AttnArgs a = slot_args(a0);
   using Lay = AsLayout<HD>;
-  constexpr int DPL = HD / 32;
-  static_assert(DPL == 2 || DPL == 4, "head_dim 64 or 128");
-  extern __shared__ __align__(1024) uint8_t as_smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(as_smem + Lay::kBarOff);
+  constexpr int R = kAsMaxRatio;
+  constexpr int KS = HD / 16;  // k-steps of Q K^T, and 16-dim column pairs of P V
+  extern __shared__ uint8_t as_raw[];
+  // tensor copies with the 128-byte swizzle land on 1024-byte boundaries
+  uint8_t* sm = as_raw + ((1024u - (smem_addr(as_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_addr(sm);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Lay::kBarOff);
   uint64_t* empty = full + kAsStages;
-  __shared__ float pbuf[kAsConsumers][R][kAttnRows];
+  __shared__ int qshift[R];
   __shared__ float wstat[kAsConsumers][R][2];
   __shared__ float red[kAsConsumers][R][HD];
   __shared__ int is_last;
@@ -80,7 +97,7 @@ __global__ void __launch_bounds__(kAsThreads) attention_stream_kernel(const __gr
   // the QKV kernel (whose consumers wait on it) let this grid launch.
   const int cur = a.st->cur_pos;
   const int n_kv = cur + 1;
-  const int n_grp = (n_kv + kAsRows - 1) / kAsRows;
+  const int n_grp = (n_kv + kAsKeys - 1) / kAsKeys;
   const int per = (n_grp + gridDim.y - 1) / gridDim.y;  // groups per split
   const int active = (n_grp + per - 1) / per;           // splits with work
   const int g0 = split * per, g1 = min(n_grp, g0 + per);
@@ -89,82 +106,195 @@ __global__ void __launch_bounds__(kAsThreads) attention_stream_kernel(const __gr
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAsStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kAsConsumers);
+      mbar_init(&empty[s], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
   if (warp == kAsConsumers) {
-    // producer: one K and one V tile per stage
+    // producer: each group's K and V halves
     if (lane == 0) {
+      const CUtensorMap* km = a0.kvmaps ? a0.kvmaps + 2 * blockIdx.z : &kmap;
+      const CUtensorMap* vm = a0.kvmaps ? a0.kvmaps + 2 * blockIdx.z + 1 : &vmap;
       uint64_t policy;
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
       bool waited = false;
       for (int g = g0, q = 0; g < g1; ++g, ++q) {
         const int s = q % kAsStages;
         if (q >= kAsStages) mbar_wait(&empty[s], (uint32_t)(((q / kAsStages) - 1) & 1));
-        if (!waited && (g + 1) * kAsRows > cur) {
-          // row cur is the QKV kernel's: request its tile after that kernel
+        if (!waited && (g + 1) * kAsKeys > cur) {
+          // row cur is the QKV kernel's: request its group after that kernel
           pdl_wait();
           asm volatile("fence.proxy.async.global;" ::: "memory");
           waited = true;
         }
-        uint8_t* dst = as_smem + s * Lay::kStage;
+        const uint32_t dst = sbase + (uint32_t)(s * Lay::kStage);
         mbar_arrive_expect_tx(&full[s], (uint32_t)Lay::kStage);
-        tma_load_tile(dst, &kmap, kh * HD, g * kAsRows, &full[s], policy);
-        tma_load_tile(dst + Lay::kTile, &vmap, kh * HD, g * kAsRows, &full[s], policy);
+#pragma unroll
+        for (int h = 0; h < Lay::kHalves; ++h) {
+          tma_load_tile(dst + h * Lay::kHalf, km, kh * HD + 64 * h, g * kAsKeys, &full[s], policy);
+          tma_load_tile(dst + Lay::kTile + h * Lay::kHalf, vm, kh * HD + 64 * h, g * kAsKeys, &full[s], policy);
+        }
       }
     }
     return;
   }
 
   // consumers
+  const int ratio = a.n_heads / a.n_kv_heads;  // <= R
+  const int tid = threadIdx.x;
+  // Q rows: 2h = hi, 2h + 1 = lo of q_h * 2^-shift_h; rows past 2 * ratio zero
+  for (int i = tid; i < Lay::kTile / 16; i += kAsConsumers * 32)
+    reinterpret_cast<uint4*>(sm + Lay::kQOff)[i] = make_uint4(0u, 0u, 0u, 0u);
   pdl_wait();
   pdl_launch_dependents();
-  const int ratio = a.n_heads / a.n_kv_heads;  // <= R
-  float qv[R][DPL];
+  consumer_bar_sync();
+  if (warp < ratio) {
+    constexpr int PL = HD / 32;  // dims per lane
+    const float* src = a.q + (size_t)(kh * ratio + warp) * HD + lane * PL;
+    float v[PL];
+    float mx = 0.0f;
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const float* qp = a.q + (size_t)(kh * ratio + r) * HD + lane * DPL;
+    for (int i = 0; i < PL; ++i) {
+      v[i] = src[i];
+      mx = fmaxf(mx, fabsf(v[i]));
+    }
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) qv[r][d] = r < ratio ? qp[d] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int sh = split_shift(mx);
+    const float in_s = ldexpf(1.0f, -sh);
+    if (lane == 0) qshift[warp] = sh;
+    uint32_t hb[PL / 2], lb[PL / 2];
+#pragma unroll
+    for (int i = 0; i < PL / 2; ++i) split2(v[2 * i] * in_s, v[2 * i + 1] * in_s, hb[i], lb[i]);
+    const int chunk = (lane * PL) / 8, within = ((lane * PL) % 8) * 2;
+    uint8_t* qh = sm + Lay::kQOff + as_off(2 * warp, chunk) + within;
+    uint8_t* ql = sm + Lay::kQOff + as_off(2 * warp + 1, chunk) + within;
+    if constexpr (PL == 4) {
+      *reinterpret_cast<uint2*>(qh) = make_uint2(hb[0], hb[1]);
+      *reinterpret_cast<uint2*>(ql) = make_uint2(lb[0], lb[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(qh) = hb[0];
+      *reinterpret_cast<uint32_t*>(ql) = lb[0];
+    }
   }
-  float m[R], l[R], acc[R][DPL];
+  consumer_bar_sync();
+  const int g8 = lane >> 2, t4 = lane & 3;  // accumulator row, column pair
+  const bool row_ok = g8 < 2 * ratio;       // rows past the heads' hi/lo pairs are zero
+  const float f = row_ok ? ldexpf(a.scale, qshift[g8 >> 1]) : 0.0f;
+  // A fragments of the Q rows for every k-step (rows 8-15 are zero)
+  uint32_t qa[KS][4];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.0f;
+  for (int kk = 0; kk < KS; ++kk)
+    ldsm_x4(sbase + Lay::kQOff + as_off((lane & 7) + ((lane >> 3) & 1) * 8, 2 * kk + (lane >> 4)), qa[kk]);
+  float o[2 * KS][4];
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) acc[r][d] = 0.0f;
-  }
-  float(*pw)[kAttnRows] = pbuf[warp];
-  const int slice = warp * kAttnRows * HD * 2 + lane * DPL * 2;  // this lane's bytes of row 0 of the slice
-  for (int g = g0, q = 0; g < g1; ++g, ++q) {
+  for (int i = 0; i < 2 * KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m = -INFINITY, l = 0.0f;
+  const int krow = (lane >> 4) * 8 + (lane & 7), kchunk = (lane >> 3) & 1;   // K: non-transposed x4
+  const int vrow = ((lane >> 3) & 1) * 8 + (lane & 7), vchunk = lane >> 4;  // V: transposed x4
+  for (int g = g0 + warp, q = warp; g < g1; g += kAsConsumers, q += kAsConsumers) {
     const int s = q % kAsStages;
     mbar_wait(&full[s], (uint32_t)((q / kAsStages) & 1));
-    const uint8_t* kt = as_smem + s * Lay::kStage + slice;
-    KvGroup<DPL> kv;
-#pragma unroll
-    for (int i = 0; i < kAttnRows; ++i) {
-      kv.k[i].load_smem(kt + i * HD * 2);
-      kv.v[i].load_smem(kt + Lay::kTile + i * HD * 2);
+    const uint32_t kst = sbase + (uint32_t)(s * Lay::kStage), vst = kst + Lay::kTile;
+    const int key0 = g * kAsKeys;
+    if (key0 + kAsKeys > n_kv) {
+      // rows past the step's own position hold old or zero bytes: clear V's
+      // (a zero probability times a non-finite value would not vanish)
+      const int nv = n_kv - key0;
+      for (int i = lane; i < (kAsKeys - nv) * Lay::kHalves * 8; i += 32) {
+        const int r = nv + i / (Lay::kHalves * 8), h = (i / 8) % Lay::kHalves, c = i % 8;
+        *reinterpret_cast<uint4*>(sm + s * Lay::kStage + Lay::kTile + h * Lay::kHalf + r * 128 + c * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
     }
-    // the rows are in registers: release the slot
+    // S = Q K^T: rows (head hi/lo) x 16 keys
+    float sc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      uint32_t b[4];
+      ldsm_x4(kst + as_off(krow, 2 * kk + kchunk), b);
+      mma16816(sc[0], qa[kk], b[0], b[1]);
+      mma16816(sc[1], qa[kk], b[2], b[3]);
+    }
+    // score of (head g8 / 2, key): the hi row plus the lo row (lanes 4 apart)
+    float x[4];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = sc[nt][e];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        const int key = key0 + nt * 8 + 2 * t4 + e;
+        v = key < n_kv ? v * f : -INFINITY;
+        x[nt * 2 + e] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m, mx);
+    const float base = mn == -INFINITY ? 0.0f : mn;
+    const float c = expf(m - base);
+    m = mn;
+    float p[4], ps = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      p[i] = expf(x[i] - base);
+      ps += p[i];
+    }
+    l = fmaf(l, c, ps);
+    if (__any_sync(0xffffffffu, row_ok && c != 1.0f)) {
+#pragma unroll
+      for (int i = 0; i < 2 * KS; ++i) {
+        o[i][0] *= c;
+        o[i][1] *= c;
+      }
+    }
+    // P as the A operand: row g8 holds the hi (even) or lo (odd) part
+    uint32_t h01, l01, h23, l23;
+    split2(p[0], p[1], h01, l01);
+    split2(p[2], p[3], h23, l23);
+    uint32_t pa[4];
+    pa[0] = row_ok ? ((g8 & 1) ? l01 : h01) : 0u;
+    pa[2] = row_ok ? ((g8 & 1) ? l23 : h23) : 0u;
+    pa[1] = pa[3] = 0u;
+    // O += P V over the 16 keys
+#pragma unroll
+    for (int dp = 0; dp < KS; ++dp) {
+      uint32_t b[4];
+      ldsm_x4_t(vst + as_off(vrow, 2 * dp + vchunk), b);
+      mma16816(o[2 * dp], pa, b[0], b[1]);
+      mma16816(o[2 * dp + 1], pa, b[2], b[3]);
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    const int j0 = g * kAsRows + warp * kAttnRows;
-    // rows past the step's own position hold old or zero bytes: never used
-#pragma unroll
-    for (int i = 0; i < kAttnRows; ++i)
-      if (j0 + i >= n_kv) {
-        kv.k[i].zero();
-        kv.v[i].zero();
-      }
-    kv_consume<DPL, R>(kv, j0, n_kv, ratio, a.scale, qv, m, l, acc, pw, lane);
   }
-  attn_finish<HD, R>(a, kh, split, active, ratio, warp, lane, m, l, acc, wstat, red, &is_last,
-                     [] { consumer_bar_sync(); });
+  // this warp's state: sum over the column lanes, then hi + lo rows
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+#pragma unroll
+  for (int i = 0; i < 2 * KS; ++i) {
+    o[i][0] += __shfl_xor_sync(0xffffffffu, o[i][0], 4);
+    o[i][1] += __shfl_xor_sync(0xffffffffu, o[i][1], 4);
+  }
+  const int h = g8 >> 1;
+  if ((g8 & 1) == 0 && h < ratio) {
+    if (t4 == 0) {
+      wstat[warp][h][0] = m;
+      wstat[warp][h][1] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < 2 * KS; ++i) {
+      red[warp][h][8 * i + 2 * t4] = o[i][0];
+      red[warp][h][8 * i + 2 * t4 + 1] = o[i][1];
+    }
+  }
+  attn_merge<HD, R>(a, kh, split, active, ratio, wstat, red, &is_last, [] { consumer_bar_sync(); });
 }
 
 // ---------------------------------------------------------------------------
@@ -188,43 +318,65 @@ inline TmapEncode tmap_encoder() {
 }
 
 // Tensor map over one layer's K (or V) cache [rows][kv_heads * hd] f16, in
-// 32-position x hd boxes; rows past the cache read as zero.
-inline CUtensorMap kv_tensor_map(const __half* cache, uint64_t rows, uint64_t span, int hd) {
+// 16-key x 64-dim boxes with the 128-byte swizzle; rows past the cache read
+// as zero.
+inline CUtensorMap kv_tensor_map(const __half* cache, uint64_t rows, uint64_t span) {
   CUtensorMap map;
   const cuuint64_t dims[2] = {span, rows};
   const cuuint64_t strides[1] = {span * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)hd, (cuuint32_t)kAsRows};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)kAsKeys};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = tmap_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(cache), dims,
-                                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   require(r == CUDA_SUCCESS, FABER_STATUS_CUDA_ERROR,
           "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return map;
 }
 
-// Splits of the streamed kernel: about kAsCtasPerSm CTAs per SM over the kv
-// heads, within the partial buffer's capacity.
-inline int attention_stream_splits(int sms, int kv_heads, int cap) {
-  return std::max(1, std::min(cap, (kAsCtasPerSm * sms + kv_heads - 1) / kv_heads));
+// Splits of the streamed kernel for `pairs` (kv head, sequence) pairs over a
+// context of up to `ctx` keys, at most `cap`: the count with the shortest
+// modelled time, waves x (a CTA's share of the pair's K/V bytes at an equal
+// share of the HBM rate + a fixed 1.5 us of start-up and merge).
+inline int attention_stream_splits(int sms, int pairs, int ctx, int hd, int cap) {
+  const double slots = (double)kAsCtasPerSm * sms;
+  const double pair_us = (double)ctx * hd * 4 / (6.5e6 / slots);  // one pair at 1/slots of 6.5 TB/s
+  int best = 1;
+  double best_t = 1e30;
+  for (int s = 1; s <= std::max(1, cap); ++s) {
+    const double waves = std::ceil((double)pairs * s / slots);
+    const double t = waves * (pair_us / s + 1.5);
+    if (t < best_t * 0.99) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
 }
 
-template <int HD, int R>
-void launch_attention_stream(const AttnArgs& a, int kv_heads, int splits, cudaStream_t stream, bool pdl) {
+template <int HD>
+void launch_attention_stream(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pdl) {
   using Lay = AsLayout<HD>;
-  auto kern = attention_stream_kernel<HD, R>;
+  auto kern = attention_stream_kernel<HD>;
   static thread_local std::map<int, bool> attr_done;
   int dev = 0;
   FABER_CUDA(cudaGetDevice(&dev));
   if (!attr_done[dev]) {
     FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes));
+    // three CTAs of about 75 KB per SM
+    FABER_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    (int)cudaSharedmemCarveoutMaxShared));
     attr_done[dev] = true;
   }
-  const uint64_t span = (uint64_t)kv_heads * HD;
-  const CUtensorMap km = kv_tensor_map(a.k, (uint64_t)a.cache_rows, span, HD);
-  const CUtensorMap vm = kv_tensor_map(a.v, (uint64_t)a.cache_rows, span, HD);
+  // a single sequence's maps travel as parameters; a batch's are in a.kvmaps
+  CUtensorMap km = {}, vm = {};
+  if (!a.kvmaps) {
+    const uint64_t span = (uint64_t)grid.x * HD;
+    km = kv_tensor_map(a.k, (uint64_t)a.cache_rows, span);
+    vm = kv_tensor_map(a.v, (uint64_t)a.cache_rows, span);
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kv_heads, splits);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(kAsThreads);
   cfg.dynamicSmemBytes = Lay::kBytes;
   cfg.stream = stream;

@@ -22,9 +22,9 @@
 #include <vector>
 
 #include "attention.cuh"
-#include "attention_stream.cuh"
 #include "bgemv.cuh"
 #include "prefill.cuh"
+#include "attention_stream.cuh"
 
 namespace faber {
 
@@ -248,12 +248,10 @@ void launch_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pd
 template <int HD>
 void launch_decode_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pdl) {
   const int ratio = a.n_heads / a.n_kv_heads;
-  if (ratio <= 2 && !a.slots && a.cache_rows > 0) {
-    const int splits = attention_stream_splits(device_info().sms, (int)grid.x, (int)grid.y);
-    if (ratio == 1)
-      launch_attention_stream<HD, 1>(a, (int)grid.x, splits, stream, pdl);
-    else
-      launch_attention_stream<HD, 2>(a, (int)grid.x, splits, stream, pdl);
+  if (ratio <= 2 && a.cache_rows > 0 && (!a.slots || a.kvmaps)) {
+    const int splits = attention_stream_splits(device_info().sms, (int)(grid.x * grid.z), a.cache_rows, HD,
+                                               (int)grid.y);
+    launch_attention_stream<HD>(a, dim3(grid.x, splits, grid.z), stream, pdl);
     return;
   }
   if (ratio < 3 || ratio > 8) {
@@ -1483,6 +1481,7 @@ struct BatchState {
   DevBuf slots;  // SlotRef [L][B]
   DevBuf h, xs, xscale, q, ctx, act, logits, attn_part, attn_counters, gen;
   DevBuf kpart;  // the batched GEMV's slab partials
+  DevBuf kvmaps;  // CUtensorMap [L][B][K, V]: the streamed attention's maps (ratio <= 2)
   cudaGraphExec_t g_step = nullptr, g_logits = nullptr;
   std::vector<int64_t> graph_eog;
   bool graphs_valid = false;
@@ -1603,6 +1602,20 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   Bt.act.alloc((size_t)n * M.Fl * 4);
   Bt.logits.alloc((size_t)n * c.vocab * 4);
   Bt.splits = attention_splits(device_info().sms, M.Hkvl * n, Bt.max_ctx);
+  if (M.Hl / M.Hkvl <= kAsMaxRatio) {
+    // the streamed attention: its split count, and every (layer, sequence)'s
+    // K and V tensor maps
+    Bt.splits = std::max(Bt.splits, attention_stream_splits(device_info().sms, M.Hkvl * n, Bt.max_ctx, hd,
+                                                            std::max(1, (Bt.max_ctx + kAsKeys - 1) / kAsKeys)));
+    std::vector<CUtensorMap> maps((size_t)c.n_layers * n * 2);
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+      for (int i = 0; i < n; ++i) {
+        maps[((size_t)l * n + i) * 2] = kv_tensor_map(refs[(size_t)l * n + i].k, (uint64_t)Bt.max_ctx, nk);
+        maps[((size_t)l * n + i) * 2 + 1] = kv_tensor_map(refs[(size_t)l * n + i].v, (uint64_t)Bt.max_ctx, nk);
+      }
+    Bt.kvmaps.alloc(maps.size() * sizeof(CUtensorMap), kLedgerConcurrent);
+    FABER_CUDA(cudaMemcpy(Bt.kvmaps.p, maps.data(), Bt.kvmaps.n, cudaMemcpyHostToDevice));
+  }
   Bt.attn_part.alloc((size_t)n * M.Hl * Bt.splits * (hd + 2) * 4);
   Bt.attn_counters.alloc((size_t)n * M.Hkvl * 4);
   FABER_CUDA(cudaMemset(Bt.attn_counters.p, 0, Bt.attn_counters.n));
@@ -1690,6 +1703,10 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.slot_q_stride = nq;
       a.slot_part_stride = M.Hl * Bt.splits * (hd + 2);
       a.slot_counter_stride = M.Hkvl;
+      if (Bt.kvmaps.p) {
+        a.cache_rows = Bt.max_ctx;
+        a.kvmaps = Bt.kvmaps.as<CUtensorMap>() + (size_t)l * n * 2;
+      }
       const dim3 grid(M.Hkvl, Bt.splits, n);
       if (hd == 128)
         launch_decode_attention<128>(a, grid, Bt.stream, false);

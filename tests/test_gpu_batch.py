@@ -6,6 +6,8 @@ lockstep: every linear layer is one batched Q4_K GEMV over all sequences
 (each exact weight fragment feeds 1, 2 or 4 MMA column blocks for up to 4, 8
 or 16 sequences; the 2816-wide down projection at 16 sequences is cut into
 two K slabs summed through the per-tile ticket).
+With one query head per kv head the step's attention is the TMA-streamed
+tensor-core kernel over each sequence's own tensor maps.
 Each sequence's tokens must equal the oracle's run_greedy for its prompt
 alone, and afterwards each session must hold its own state: its
 position_logits equal the oracle's logits that chose its last token
@@ -68,6 +70,40 @@ def test_batch_greedy_matches_oracle(pair, lengths):
     more, ok = runs[0].greedy(3)
     ref_more, _, _ = om.greedy(prompts[0], N_GEN + 2)
     assert ok and more.tolist() == ref_more[N_GEN - 1:].tolist()
+    batch.close()
+    for r in runs:
+        r.close()
+
+
+@pytest.fixture(scope="module")
+def mha_pair(cuda):
+    import oracle as o
+    from faber_runtime_b200 import DeviceModel, synth
+    cfg = _cfg(kv_heads=8, head_dim=128, heads=8)
+    tensors = list(synth.model_tensors(cfg, 67, norms="random"))
+    om = o.OracleModel(cfg, {n: (t, a, r, c) for n, t, a, r, c in tensors})
+    return cfg, om, DeviceModel(cfg, tensors)
+
+
+@pytest.mark.parametrize("lengths", [
+    [40, 7, 100, 33, 64],
+    [33 + 3 * i for i in range(16)],
+])
+def test_batch_mha_greedy_matches_oracle(mha_pair, lengths):
+    """One query head per kv head: the batched step's attention runs on the
+    TMA-streamed tensor-core kernel with every sequence's own K/V tensor
+    maps (grid.z = sequence)."""
+    from faber_runtime_b200 import BatchRun, ForwardRun, synth
+    cfg, om, dm = mha_pair
+    prompts = [synth.tokens(67, 200 + i, n, cfg.vocab) for i, n in enumerate(lengths)]
+    runs = [ForwardRun(dm, p, context_length=max(lengths) + N_GEN + 8) for p in prompts]
+    batch = BatchRun(runs)
+    toks, fin = batch.greedy(N_GEN)
+    assert fin.all()
+    for i, p in enumerate(prompts):
+        ref_tokens, ref_logits, _ = om.greedy(p, N_GEN, want_logits=True)
+        assert toks[i].tolist() == ref_tokens.tolist(), (i, toks[i].tolist(), ref_tokens.tolist())
+        within(runs[i].position_logits(), ref_logits[N_GEN - 1])
     batch.close()
     for r in runs:
         r.close()
