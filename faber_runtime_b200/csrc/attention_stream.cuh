@@ -1,6 +1,6 @@
-// attention_stream.cuh — decode attention for up to two query heads per kv
-// head (the Llama-2-7B step is one), K/V tiles streamed into shared memory by
-// TMA, scores and context on the tensor cores (attention_gqa,
+// attention_stream.cuh — decode attention for up to eight query heads per kv
+// head (Llama-2-7B: one, Llama-3-70B: eight), K/V tiles streamed into shared
+// memory by TMA, scores and context on the tensor cores (attention_gqa,
 // src/cpu_oracle.rs:711-792, for one query row).
 //
 //   * grid (kv heads, splits, sequences), three CTAs per SM, the split count
@@ -16,7 +16,8 @@
 //     during the tail of the QKV kernel; the group holding row cur after it;
 //   * consumer warp w takes groups w, w + 4, ... Each query head is split
 //     exactly into f16 hi and lo rows (per-head power-of-two scale) of the
-//     MMA A operand: S = Q K^T on m16n8k16 (8 k-steps per 16 keys at head_dim
+//     MMA A operand, 16 rows for up to 8 heads, so the grouping costs no
+//     extra MMAs: S = Q K^T on m16n8k16 (8 k-steps per 16 keys at head_dim
 //     128), score = (S_hi + S_lo) * scale; an online softmax per warp; the
 //     probabilities, split into hi/lo rows the same way, multiply V (the
 //     score accumulator's layout is the A fragment's), so both products keep
@@ -41,7 +42,11 @@ constexpr int kAsStages = 8;
 constexpr int kAsConsumers = kAttnWarps;             // 4 consumer warps
 constexpr int kAsThreads = (kAsConsumers + 1) * 32;  // + the producer warp
 constexpr int kAsCtasPerSm = 3;
-constexpr int kAsMaxRatio = 2;
+constexpr int kAsMaxRatio = 8;  // 16 MMA rows: each query head's hi and lo
+// Groupings the decode step routes here. Up to 8 heads are exact here too,
+// but at 8 (the 70B shape) the last CTA's merge of ratio x head_dim outputs
+// over up to 55 splits costs more than this kernel saves.
+constexpr int kAsStreamMaxRatio = 2;
 
 template <int HD>
 struct AsLayout {
@@ -73,6 +78,39 @@ __device__ __forceinline__ void consumer_bar_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kAsConsumers * 32) : "memory");
 }
 
+// Online-softmax update of one accumulator row half over a stage's 16 keys.
+// s00, s01 / s10, s11: this lane's accumulator values of keys 2 t4, 2 t4 + 1
+// / 8 + 2 t4, 9 + 2 t4 in its row; the row's hi and lo partner (4 lanes away)
+// adds in, f scales the sum to a score, keys from n_kv on are masked. Returns
+// the rescale of the running state; p receives the probabilities.
+__device__ __forceinline__ float as_softmax(float s00, float s01, float s10, float s11, float f, int key0,
+                                            int t4, int n_kv, float& m, float& l, float (&p)[4]) {
+  float x[4] = {s00, s01, s10, s11};
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float v = x[i] + __shfl_xor_sync(0xffffffffu, x[i], 4);
+    const int key = key0 + (i >> 1) * 8 + 2 * t4 + (i & 1);
+    v = key < n_kv ? v * f : -INFINITY;
+    x[i] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float mn = fmaxf(m, mx);
+  const float base = mn == -INFINITY ? 0.0f : mn;
+  const float c = expf(m - base);
+  m = mn;
+  float ps = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    p[i] = expf(x[i] - base);
+    ps += p[i];
+  }
+  l = fmaf(l, c, ps);
+  return c;
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
     attention_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -89,7 +127,6 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
   uint64_t* empty = full + kAsStages;
   __shared__ int qshift[R];
   __shared__ float wstat[kAsConsumers][R][2];
-  __shared__ float red[kAsConsumers][R][HD];
   __shared__ int is_last;
 
   const int kh = blockIdx.x, split = blockIdx.y;
@@ -150,9 +187,9 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
   pdl_wait();
   pdl_launch_dependents();
   consumer_bar_sync();
-  if (warp < ratio) {
+  for (int hq = warp; hq < ratio; hq += kAsConsumers) {
     constexpr int PL = HD / 32;  // dims per lane
-    const float* src = a.q + (size_t)(kh * ratio + warp) * HD + lane * PL;
+    const float* src = a.q + (size_t)(kh * ratio + hq) * HD + lane * PL;
     float v[PL];
     float mx = 0.0f;
 #pragma unroll
@@ -164,13 +201,13 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const int sh = split_shift(mx);
     const float in_s = ldexpf(1.0f, -sh);
-    if (lane == 0) qshift[warp] = sh;
+    if (lane == 0) qshift[hq] = sh;
     uint32_t hb[PL / 2], lb[PL / 2];
 #pragma unroll
     for (int i = 0; i < PL / 2; ++i) split2(v[2 * i] * in_s, v[2 * i + 1] * in_s, hb[i], lb[i]);
     const int chunk = (lane * PL) / 8, within = ((lane * PL) % 8) * 2;
-    uint8_t* qh = sm + Lay::kQOff + as_off(2 * warp, chunk) + within;
-    uint8_t* ql = sm + Lay::kQOff + as_off(2 * warp + 1, chunk) + within;
+    uint8_t* qh = sm + Lay::kQOff + as_off(2 * hq, chunk) + within;
+    uint8_t* ql = sm + Lay::kQOff + as_off(2 * hq + 1, chunk) + within;
     if constexpr (PL == 4) {
       *reinterpret_cast<uint2*>(qh) = make_uint2(hb[0], hb[1]);
       *reinterpret_cast<uint2*>(ql) = make_uint2(lb[0], lb[1]);
@@ -180,10 +217,14 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
     }
   }
   consumer_bar_sync();
-  const int g8 = lane >> 2, t4 = lane & 3;  // accumulator row, column pair
-  const bool row_ok = g8 < 2 * ratio;       // rows past the heads' hi/lo pairs are zero
-  const float f = row_ok ? ldexpf(a.scale, qshift[g8 >> 1]) : 0.0f;
-  // A fragments of the Q rows for every k-step (rows 8-15 are zero)
+  // Accumulator rows of this lane: g8 (head g8 / 2) and g8 + 8 (head 4 + g8 / 2),
+  // hi rows even, lo rows odd; rows past the heads' pairs are zero.
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const bool hi8 = ratio > 4;  // heads in rows 8-15 (warp-uniform)
+  const bool ok_a = g8 < 2 * ratio, ok_b = g8 + 8 < 2 * ratio;
+  const float f_a = ok_a ? ldexpf(a.scale, qshift[g8 >> 1]) : 0.0f;
+  const float f_b = ok_b ? ldexpf(a.scale, qshift[4 + (g8 >> 1)]) : 0.0f;
+  // A fragments of the Q rows for every k-step
   uint32_t qa[KS][4];
 #pragma unroll
   for (int kk = 0; kk < KS; ++kk)
@@ -191,7 +232,7 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
   float o[2 * KS][4];
 #pragma unroll
   for (int i = 0; i < 2 * KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-  float m = -INFINITY, l = 0.0f;
+  float m_a = -INFINITY, l_a = 0.0f, m_b = -INFINITY, l_b = 0.0f;
   const int krow = (lane >> 4) * 8 + (lane & 7), kchunk = (lane >> 3) & 1;   // K: non-transposed x4
   const int vrow = ((lane >> 3) & 1) * 8 + (lane & 7), vchunk = lane >> 4;  // V: transposed x4
   for (int g = g0 + warp, q = warp; g < g1; g += kAsConsumers, q += kAsConsumers) {
@@ -221,48 +262,32 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
       mma16816(sc[0], qa[kk], b[0], b[1]);
       mma16816(sc[1], qa[kk], b[2], b[3]);
     }
-    // score of (head g8 / 2, key): the hi row plus the lo row (lanes 4 apart)
-    float x[4];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float v = sc[nt][e];
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        const int key = key0 + nt * 8 + 2 * t4 + e;
-        v = key < n_kv ? v * f : -INFINITY;
-        x[nt * 2 + e] = v;
-        mx = fmaxf(mx, v);
-      }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float mn = fmaxf(m, mx);
-    const float base = mn == -INFINITY ? 0.0f : mn;
-    const float c = expf(m - base);
-    m = mn;
-    float p[4], ps = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      p[i] = expf(x[i] - base);
-      ps += p[i];
-    }
-    l = fmaf(l, c, ps);
-    if (__any_sync(0xffffffffu, row_ok && c != 1.0f)) {
+    float p_a[4], p_b[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const float c_a = as_softmax(sc[0][0], sc[0][1], sc[1][0], sc[1][1], f_a, key0, t4, n_kv, m_a, l_a, p_a);
+    float c_b = 1.0f;
+    if (hi8) c_b = as_softmax(sc[0][2], sc[0][3], sc[1][2], sc[1][3], f_b, key0, t4, n_kv, m_b, l_b, p_b);
+    if (__any_sync(0xffffffffu, (ok_a && c_a != 1.0f) || (ok_b && c_b != 1.0f))) {
 #pragma unroll
       for (int i = 0; i < 2 * KS; ++i) {
-        o[i][0] *= c;
-        o[i][1] *= c;
+        o[i][0] *= c_a;
+        o[i][1] *= c_a;
+        o[i][2] *= c_b;
+        o[i][3] *= c_b;
       }
     }
-    // P as the A operand: row g8 holds the hi (even) or lo (odd) part
-    uint32_t h01, l01, h23, l23;
-    split2(p[0], p[1], h01, l01);
-    split2(p[2], p[3], h23, l23);
+    // P as the A operand: each row holds the hi (even) or lo (odd) part
     uint32_t pa[4];
-    pa[0] = row_ok ? ((g8 & 1) ? l01 : h01) : 0u;
-    pa[2] = row_ok ? ((g8 & 1) ? l23 : h23) : 0u;
-    pa[1] = pa[3] = 0u;
+    {
+      uint32_t h01, l01, h23, l23;
+      split2(p_a[0], p_a[1], h01, l01);
+      split2(p_a[2], p_a[3], h23, l23);
+      pa[0] = ok_a ? ((g8 & 1) ? l01 : h01) : 0u;
+      pa[2] = ok_a ? ((g8 & 1) ? l23 : h23) : 0u;
+      split2(p_b[0], p_b[1], h01, l01);
+      split2(p_b[2], p_b[3], h23, l23);
+      pa[1] = ok_b ? ((g8 & 1) ? l01 : h01) : 0u;
+      pa[3] = ok_b ? ((g8 & 1) ? l23 : h23) : 0u;
+    }
     // O += P V over the 16 keys
 #pragma unroll
     for (int dp = 0; dp < KS; ++dp) {
@@ -275,23 +300,31 @@ __global__ void __launch_bounds__(kAsThreads, kAsCtasPerSm)
     if (lane == 0) mbar_arrive(&empty[s]);
   }
   // this warp's state: sum over the column lanes, then hi + lo rows
-  l += __shfl_xor_sync(0xffffffffu, l, 1);
-  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
 #pragma unroll
-  for (int i = 0; i < 2 * KS; ++i) {
-    o[i][0] += __shfl_xor_sync(0xffffffffu, o[i][0], 4);
-    o[i][1] += __shfl_xor_sync(0xffffffffu, o[i][1], 4);
-  }
-  const int h = g8 >> 1;
-  if ((g8 & 1) == 0 && h < ratio) {
-    if (t4 == 0) {
-      wstat[warp][h][0] = m;
-      wstat[warp][h][1] = l;
-    }
+  for (int i = 0; i < 2 * KS; ++i)
 #pragma unroll
-    for (int i = 0; i < 2 * KS; ++i) {
-      red[warp][h][8 * i + 2 * t4] = o[i][0];
-      red[warp][h][8 * i + 2 * t4 + 1] = o[i][1];
+    for (int e = 0; e < 4; ++e) o[i][e] += __shfl_xor_sync(0xffffffffu, o[i][e], 4);
+  // every warp is done with the ring: the warps' contexts go there
+  consumer_bar_sync();
+  auto& red = *reinterpret_cast<float(*)[kAsConsumers][R][HD]>(sm);
+  if ((g8 & 1) == 0) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int h = (g8 >> 1) + 4 * half;
+      if (h >= ratio) continue;
+      if (t4 == 0) {
+        wstat[warp][h][0] = half ? m_b : m_a;
+        wstat[warp][h][1] = half ? l_b : l_a;
+      }
+#pragma unroll
+      for (int i = 0; i < 2 * KS; ++i) {
+        red[warp][h][8 * i + 2 * t4] = o[i][2 * half];
+        red[warp][h][8 * i + 2 * t4 + 1] = o[i][2 * half + 1];
+      }
     }
   }
   attn_merge<HD, R>(a, kh, split, active, ratio, wstat, red, &is_last, [] { consumer_bar_sync(); });

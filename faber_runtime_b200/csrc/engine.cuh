@@ -240,21 +240,23 @@ void launch_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pd
     launch_pdl(attention_decode_kernel<HD, 8>, grid, block, 0, stream, pdl, a);
 }
 
-// Decode attention of a step: grouped heads (ratio 3..8) on the tensor cores,
-// one wave of CTAs (kv heads x sequences x splits, the split count within the
-// session's partial buffer); one or two query heads per kv head of a single
-// sequence on the TMA-streamed kernel; batched sequences of those ratios on
-// the register-streamed CUDA-core kernel.
+// Decode attention of a step: one or two query heads per kv head on the
+// TMA-streamed tensor-core kernel (a batch through its sequences' tensor
+// maps), with the split count from its wave model within the partial
+// buffer's capacity grid.y; grouped heads (ratio 3..8) on the tensor-core GQA
+// kernel, one wave of CTAs (kv heads x sequences x splits).
 template <int HD>
 void launch_decode_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, bool pdl) {
   const int ratio = a.n_heads / a.n_kv_heads;
-  if (ratio <= 2 && a.cache_rows > 0 && (!a.slots || a.kvmaps)) {
+  if (ratio <= kAsStreamMaxRatio) {
+    require(a.cache_rows > 0 && (!a.slots || a.kvmaps), FABER_STATUS_UNSUPPORTED,
+            "decode attention needs the cache extent (and a batch its tensor maps)");
     const int splits = attention_stream_splits(device_info().sms, (int)(grid.x * grid.z), a.cache_rows, HD,
                                                (int)grid.y);
     launch_attention_stream<HD>(a, dim3(grid.x, splits, grid.z), stream, pdl);
     return;
   }
-  if (ratio < 3 || ratio > 8) {
+  if (ratio > 8) {
     launch_attention<HD>(a, grid, stream, pdl);
     return;
   }
@@ -1602,7 +1604,7 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
   Bt.act.alloc((size_t)n * M.Fl * 4);
   Bt.logits.alloc((size_t)n * c.vocab * 4);
   Bt.splits = attention_splits(device_info().sms, M.Hkvl * n, Bt.max_ctx);
-  if (M.Hl / M.Hkvl <= kAsMaxRatio) {
+  if (M.Hl / M.Hkvl <= kAsStreamMaxRatio) {
     // the streamed attention: its split count, and every (layer, sequence)'s
     // K and V tensor maps
     Bt.splits = std::max(Bt.splits, attention_stream_splits(device_info().sms, M.Hkvl * n, Bt.max_ctx, hd,
@@ -1703,10 +1705,8 @@ inline void enqueue_batch_push(BatchState& Bt) {
       a.slot_q_stride = nq;
       a.slot_part_stride = M.Hl * Bt.splits * (hd + 2);
       a.slot_counter_stride = M.Hkvl;
-      if (Bt.kvmaps.p) {
-        a.cache_rows = Bt.max_ctx;
-        a.kvmaps = Bt.kvmaps.as<CUtensorMap>() + (size_t)l * n * 2;
-      }
+      a.cache_rows = Bt.max_ctx;
+      if (Bt.kvmaps.p) a.kvmaps = Bt.kvmaps.as<CUtensorMap>() + (size_t)l * n * 2;
       const dim3 grid(M.Hkvl, Bt.splits, n);
       if (hd == 128)
         launch_decode_attention<128>(a, grid, Bt.stream, false);
