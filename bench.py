@@ -391,7 +391,8 @@ def run_faber(args):
     peak, peak_kind = peaks()
     step_bytes = (cfg.linear_bytes() + cfg.head_bytes()) / ws + \
         cfg.kv_bytes_per_position() * (PREFILL + args.warmup + args.steps / 2) / ws
-    launches_per_token = (5 * cfg.n_layers + 3) if ws == 1 else (5 * cfg.n_layers + 3)
+    # per layer QKV, attention, O, gate/up, down; per token embed, head, finalize
+    launches_per_token = 5 * cfg.n_layers + 3
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": n, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "f32",
