@@ -251,7 +251,7 @@ void launch_decode_attention(const AttnArgs& a, dim3 grid, cudaStream_t stream, 
   if (ratio <= kAsStreamMaxRatio) {
     require(a.cache_rows > 0 && (!a.slots || a.kvmaps), FABER_STATUS_UNSUPPORTED,
             "decode attention needs the cache extent (and a batch its tensor maps)");
-    const int splits = attention_stream_splits(device_info().sms, (int)(grid.x * grid.z), a.cache_rows, HD,
+    const int splits = attention_stream_splits(device_info().sms, (int)(grid.x * grid.z), a.cache_rows, HD, ratio,
                                                (int)grid.y);
     launch_attention_stream<HD>(a, dim3(grid.x, splits, grid.z), stream, pdl);
     return;
@@ -1608,6 +1608,7 @@ inline void batch_build(BatchState& Bt, SessionState* const* seqs, int n) {
     // the streamed attention: its split count, and every (layer, sequence)'s
     // K and V tensor maps
     Bt.splits = std::max(Bt.splits, attention_stream_splits(device_info().sms, M.Hkvl * n, Bt.max_ctx, hd,
+                                                            M.Hl / M.Hkvl,
                                                             std::max(1, (Bt.max_ctx + kAsKeys - 1) / kAsKeys)));
     std::vector<CUtensorMap> maps((size_t)c.n_layers * n * 2);
     for (uint32_t l = 0; l < c.n_layers; ++l)
