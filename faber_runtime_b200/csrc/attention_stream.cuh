@@ -1,7 +1,8 @@
-// attention_stream.cuh — decode attention for up to eight query heads per kv
-// head (Llama-2-7B: one, Llama-3-70B: eight), K/V tiles streamed into shared
+// attention_stream.cuh — decode attention with K/V tiles streamed into shared
 // memory by TMA, scores and context on the tensor cores (attention_gqa,
-// src/cpu_oracle.rs:711-792, for one query row).
+// src/cpu_oracle.rs:711-792, for one query row). Exact for up to eight query
+// heads per kv head; the decode step routes one or two here (the Llama-2-7B
+// shape has one), see kAsStreamMaxRatio.
 //
 //   * grid (kv heads, splits, sequences), three CTAs per SM, the split count
 //     chosen from the launch's shape (attention_stream_splits); CTA (kh,
