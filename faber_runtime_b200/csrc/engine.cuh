@@ -1043,9 +1043,9 @@ inline void enqueue_logits(SessionState& S, bool pdl, const std::vector<int64_t>
 
 // A device-side bounded wait that expired (pipeline stage or tensor-parallel
 // peer) is reported once the step has run; the flag is cleared.
-inline void check_device_waits() {
-  int err = 0;
-  FABER_CUDA(cudaMemcpyFromSymbol(&err, g_pipe_error, sizeof(int)));
+// Turns a recorded wait expiry (g_pipe_error, read by the caller) into its
+// status, clearing the record.
+inline void raise_device_wait(int err) {
   if (!err) return;
   const int zero = 0;
   FABER_CUDA(cudaMemcpyToSymbol(g_pipe_error, &zero, sizeof(int)));
@@ -1053,6 +1053,12 @@ inline void check_device_waits() {
               err == 2   ? "a tensor-parallel peer did not publish its partials in time"
               : err == 3 ? "a grid barrier wait expired"
                          : "a device pipeline wait expired");
+}
+
+inline void check_device_waits() {
+  int err = 0;
+  FABER_CUDA(cudaMemcpyFromSymbol(&err, g_pipe_error, sizeof(int)));
+  raise_device_wait(err);
 }
 
 // After a step whose device work failed (a bounded wait expired, or a
@@ -1457,8 +1463,11 @@ inline int64_t run_step_greedy(SessionState& S, int64_t token, const int64_t* eo
     FABER_CUDA(cudaGraphLaunch(S.g_step, S.stream));
   }
   FABER_CUDA(cudaMemcpyAsync(pin + 1, &st->input_token, 8, cudaMemcpyDeviceToHost, S.stream));
+  // the wait-expiry record comes back with the token: one round trip
+  pin[2] = 0;
+  FABER_CUDA(cudaMemcpyFromSymbolAsync(pin + 2, g_pipe_error, sizeof(int), 0, cudaMemcpyDeviceToHost, S.stream));
   FABER_CUDA(cudaStreamSynchronize(S.stream));
-  check_device_waits();
+  raise_device_wait(static_cast<int>(pin[2]));
   S.n += 1;
   S.h_valid = true;
   });
