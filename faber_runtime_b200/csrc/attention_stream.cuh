@@ -371,9 +371,10 @@ inline CUtensorMap kv_tensor_map(const __half* cache, uint64_t rows, uint64_t sp
 // Splits of the streamed kernel for `pairs` (kv head, sequence) pairs of
 // `ratio` query heads over a context of up to `ctx` keys, at most `cap`: the
 // count with the shortest modelled time, waves x (a CTA's share of the
-// pair's K/V bytes at an equal share of the HBM rate + 1.5 us of start-up
-// and partial write) + the last CTA's merge (one 0.7 us round trip per 16
-// splits for every 128 outputs a thread produces).
+// pair's K/V bytes at an equal share of the HBM rate + 3 us of start-up and
+// partial write) + the last CTA's merge (one 0.7 us round trip per 16 splits
+// for every 128 outputs a thread produces). Measured on the 7B shape: 13
+// splits at batch 1 (9: 0.6% slower, 18: 7.6%), 4 at batch 16 (5: 1%, 6: 3.6%).
 inline int attention_stream_splits(int sms, int pairs, int ctx, int hd, int ratio, int cap) {
   const double slots = (double)kAsCtasPerSm * sms;
   const double pair_us = (double)ctx * hd * 4 / (6.5e6 / slots);  // one pair at 1/slots of 6.5 TB/s
@@ -382,7 +383,7 @@ inline int attention_stream_splits(int sms, int pairs, int ctx, int hd, int rati
   double best_t = 1e30;
   for (int s = 1; s <= std::max(1, cap); ++s) {
     const double waves = std::ceil((double)pairs * s / slots);
-    const double t = waves * (pair_us / s + 1.5) + std::ceil(s / 16.0) * outputs * 0.7;
+    const double t = waves * (pair_us / s + 3.0) + std::ceil(s / 16.0) * outputs * 0.7;
     if (t < best_t * 0.99) {
       best_t = t;
       best = s;
